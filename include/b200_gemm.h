@@ -1,0 +1,81 @@
+/*
+ * b200_gemm.h - C ABI of the B200 (sm_100a) FP16 GEMM library
+ * (libb200gemm.so).  Plain pointers, sizes and a stream handle; no C++ or
+ * torch types, so it binds from ctypes, cffi, cgo or JNI alike.
+ *
+ * Numerics: C = A * B with fp16 inputs, an fp32 accumulator and one
+ * round-to-nearest-even conversion to fp16 per output element (alpha = 1,
+ * beta = 0), the arithmetic of the reference kernels' epilogue
+ * (tensorcore_gemm/gemm.cu:1360-1361).
+ *
+ * Layouts (all row-major with a leading dimension in ELEMENTS):
+ *   A  M x K, element (i, k) at A[i * lda + k]
+ *   B  b_layout = B200_B_ROW_MAJOR: K x N, element (k, j) at B[k * ldb + j]
+ *      b_layout = B200_B_COL_MAJOR: stored N x K ("colb", pre-transposed),
+ *                 element (k, j) at B[j * ldb + k]
+ *   C  M x N, element (i, j) at C[i * ldc + j]
+ *
+ * Requirements (TMA): every base pointer 16-byte aligned and every leading
+ * dimension a multiple of 8 elements (16 bytes).  Any M, N, K >= 0 is
+ * accepted; no M/N/K divisibility is required.
+ */
+#ifndef B200_GEMM_H_
+#define B200_GEMM_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_B_ROW_MAJOR 0
+#define B200_B_COL_MAJOR 1
+
+/* Return codes. */
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad layout, ld too small */
+#define B200_ERR_MISALIGNED 2       /* base pointer not 16 B aligned or ld not a multiple of 8 */
+#define B200_ERR_TOO_LARGE 3        /* a dimension beyond 2^31 - 1 */
+#define B200_ERR_CUDA 4             /* a CUDA runtime call or the kernel launch failed */
+#define B200_ERR_TENSOR_MAP 5       /* cuTensorMapEncodeTiled unavailable or rejected the map */
+#define B200_ERR_DEVICE 6           /* the device error word was set (a bounded wait timed out) */
+#define B200_ERR_UNSUPPORTED_DEVICE 7 /* current device is not sm_100 */
+
+/*
+ * C = A * B on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Asynchronous: returns after the launch.  Replaces the reference's native
+ * entry `root_gemm_cuda(A, B, mode)` (tensorcore_gemm/gemm.py:32-153): mode
+ * ids 2/3 there are b_layout = B200_B_ROW_MAJOR here, mode ids 4/5
+ * (`use_colb`, gemm.py:43) are B200_B_COL_MAJOR.  Unlike the reference the
+ * caller owns C (the reference allocated it with torch::empty, gemm.py:61).
+ */
+B200_API int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                  int64_t ldb, int64_t ldc, int b_layout, void* stream);
+
+/* Human-readable text of a return code (static storage). Counterpart of the
+ * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */
+B200_API const char* b200_gemm_strerror(int code);
+
+/* Reads and clears the device error word of the current device (0 = none;
+ * see DeviceError in csrc/sm100_ptx.cuh).  Synchronises the device.  No
+ * counterpart in the reference, whose kernels have no bounded waits. */
+B200_API int b200_gemm_last_device_error(void);
+
+/* Number of SMs the persistent scheduler launches on for the current device
+ * (0 on error).  No counterpart in the reference. */
+B200_API int b200_gemm_sm_count(void);
+
+/* Library ABI version (major * 100 + minor). */
+B200_API int b200_gemm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_GEMM_H_ */
