@@ -1,0 +1,467 @@
+"""Benchmark of the FP16 GEMM hot path on B200 (one process per GPU).
+
+Workload: C = A @ B with M = 65536, N = K = 8192, A and B
+iid N(0, 0.02) fp16, A row-sharded over the N GPUs, B replicated; fp32
+accumulation, fp16 output.  One step = one pass of the GEMM over this rank's
+shard (strong scaling: total work fixed).  The inputs (A shard >= 128 MiB +
+B 128 MiB per GPU) exceed the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints ONE JSON line on rank 0.  `value` is the whole-job TFLOP/s from CUDA
+events (max over ranks); `e2e` times the public API with the operands in
+pinned host memory (H2D of A shard + B, GEMM, D2H of C inside the timed
+region).  At N=1 rank 0 also reports the skinny K=256 shape's HBM bandwidth,
+the 8192^3 shapes in both B layouts, and torch.mm on the same box, plus the
+reference's CPU path timed on a bounded sample.
+
+`--impl reference` runs the unmodified reference package (installed under
+baseline/_ref) through its public `tensorcore_gemm.gemm` on CPU tensors: its
+CPU path, `torch.matmul` in fp16 (tensorcore_gemm/gemm.py:219-221), timed on
+a bounded row slice of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG_DIR = REPO / "ampere-gemm_b200"
+REF_DIR = REPO / "baseline" / "_ref"
+
+M_TOTAL, N_DIM, K_DIM = 65536, 8192, 8192
+STD = 0.02
+SKINNY = (32768, 1024, 256)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-extras", action="store_true", help="skip the N=1 side measurements")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# nvidia-smi clock sampling during the timed region
+# ---------------------------------------------------------------------------
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.05)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Reference CPU path (bounded samples of the same workload)
+# ---------------------------------------------------------------------------
+def load_reference_package():
+    """The unmodified reference package from baseline/_ref, under its own name."""
+    import importlib.util
+
+    init = REF_DIR / "tensorcore_gemm" / "__init__.py"
+    if not init.exists():
+        return None
+    spec = importlib.util.spec_from_file_location(
+        "_reference_tensorcore_gemm", init, submodule_search_locations=[str(init.parent)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class CpuBaseline:
+    """Times the reference's CPU implementation on a row slice of the workload.
+
+    kind "reference": the reference's public gemm() on CPU tensors, i.e. its
+    torch.matmul fp16 fallback (tensorcore_gemm/gemm.py:219-221), with every
+    host thread.  kind "port": the C oracle, if the reference is not installed.
+    """
+
+    def __init__(self, target_s: float = 2.0):
+        import torch
+
+        self.torch = torch
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
+        self.ref = load_reference_package()
+        self.kind = "reference" if self.ref is not None else "port"
+        g = torch.Generator().manual_seed(1)
+        self.B = (torch.randn((K_DIM, N_DIM), generator=g) * STD).half()
+        self.rows = 64
+        self.A = self._a(self.rows)
+        for _ in range(3):                   # grow the slice until one step takes ~target_s
+            t = self.step()
+            if t >= 0.6 * target_s or self.rows >= 8192:
+                break
+            rows = int(self.rows * target_s / max(t, 1e-3))
+            self.rows = max(64, min(8192, rows // 64 * 64))
+            self.A = self._a(self.rows)
+
+    def _a(self, rows):
+        g = self.torch.Generator().manual_seed(0)
+        return (self.torch.randn((rows, K_DIM), generator=g) * STD).half()
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            C = self.ref.gemm(self.A, self.B, mode="reg_pingpong_256")
+        else:
+            sys.path.insert(0, str(REPO))
+            from oracle import oracle
+            C, _ = oracle.gemm_f16(self.A.numpy(), self.B.numpy(), threads=self.cores, want_acc=False)
+        assert C.shape[0] == self.rows
+        return time.perf_counter() - t0
+
+    def flops(self) -> float:
+        return 2.0 * self.rows * N_DIM * K_DIM
+
+    def sample(self) -> str:
+        path = ("reference tensorcore_gemm.gemm on CPU tensors (torch.matmul fp16 fallback)"
+                if self.kind == "reference" else "C oracle port")
+        return (f"{self.rows} x {N_DIM} x {K_DIM} row slice of the {M_TOTAL} x {N_DIM} x {K_DIM} workload; "
+                f"{path}; {self.cores} threads; {cpu_model()}")
+
+    def measure(self, reps: int = 3) -> dict:
+        ts = sorted(self.step() for _ in range(reps))
+        t = ts[len(ts) // 2]
+        return {"value": round(self.flops() / t / 1e12, 5), "unit": "TFLOP/s", "cores": self.cores,
+                "kind": self.kind, "sample": self.sample() + f"; median of {reps}"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0  # the reference is a single-process CPU path: rank 0 alone runs it
+    cpu = CpuBaseline(target_s=2.0)
+    for _ in range(max(args.warmup, 0)):
+        cpu.step()
+    times = [cpu.step() for _ in range(args.steps)]
+    total = sum(times)
+    value = cpu.flops() * args.steps / total / 1e12
+    line = {
+        "impl": "reference",
+        "metric": BASELINE_METRIC, "value": round(value, 5), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 in / f32 accumulate (CPU torch.matmul)",
+        "data": "synthetic N(0,0.02) fp16, seeded", "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cpu.cores, "kind": cpu.kind,
+                         "sample": cpu.sample()},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+BASELINE_METRIC = "FP16 GEMM TFLOPS/GPU & % dense tensor peak; HBM GB/s at K=256; box TFLOPS 1-8"
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {"workload": f"fp16_gemm_{M_TOTAL}x{N_DIM}x{K_DIM}_A_row_sharded",
+            "M": M_TOTAL, "N": N_DIM, "K": K_DIM, "b_layout": "row-major K x N",
+            "inputs": "A, B iid N(0, 0.02) fp16", "parallelism": f"A row-sharded over {n_gpus} GPU(s), B replicated",
+            "global_batch": M_TOTAL, "l2": "inputs larger than L2 (A shard + B >= 256 MiB per GPU); no flush"}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def _time_launches(torch, fn, iters: int) -> float:
+    """Mean ms per call of fn() over `iters` back-to-back calls (CUDA events)."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def read_traffic_per_launch(tag: str):
+    """DRAM bytes per full launch recorded from an ncu capture under profiles/."""
+    for p in sorted((REPO / "profiles").glob("*.md")):
+        for line in p.read_text().splitlines():
+            if line.startswith(f"traffic_bytes_per_launch[{tag}]:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip().split()[0]))
+                except ValueError:
+                    return None
+    return None
+
+
+def side_measurements(torch, tg, dev, peaks) -> dict:
+    """N=1 only: skinny K=256 HBM bandwidth (cold L2), 8192^3 both layouts, torch.mm."""
+    out = {}
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    # --- skinny: rotate buffer sets so every launch reads A and writes C from/to HBM
+    M, N, K = SKINNY
+    set_bytes = 2 * (M * K + K * N + M * N)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nsets = max(2, -(-2 * l2 // set_bytes))
+    g = torch.Generator(device=dev).manual_seed(7)
+    sets = [(torch.randn((M, K), generator=g, device=dev, dtype=torch.float16),
+             torch.randn((K, N), generator=g, device=dev, dtype=torch.float16),
+             torch.empty((M, N), device=dev, dtype=torch.float16)) for _ in range(nsets)]
+    bcol = [b.t().contiguous() for _, b, _ in sets]
+    row = lambda i: tg.gemm(sets[i % nsets][0], sets[i % nsets][1], out=sets[i % nsets][2])
+    col = lambda i: tg.gemm_pretransposed(sets[i % nsets][0], bcol[i % nsets], mode="reg_pingpong_256_colb")
+    mm = lambda i: torch.mm(sets[i % nsets][0], sets[i % nsets][1], out=sets[i % nsets][2])
+    for f in (row, col, mm):
+        for i in range(3 * nsets):
+            f(i)
+    iters = 40 * nsets
+    ms_row = _time_launches(torch, row, iters)
+    ms_col = _time_launches(torch, col, iters)
+    ms_mm = _time_launches(torch, mm, iters)
+    gbs = lambda ms: set_bytes / (ms * 1e-3) / 1e9
+    out["skinny_32768x1024x256"] = {
+        "cold_l2": f"{nsets} rotating operand sets of {set_bytes / 1e6:.1f} MB (> 2x L2)",
+        "algorithmic_bytes": set_bytes,
+        "rowB_us": round(ms_row * 1e3, 2), "rowB_GBps": round(gbs(ms_row), 1),
+        "colb_us": round(ms_col * 1e3, 2), "colb_GBps": round(gbs(ms_col), 1),
+        "torch_mm_us": round(ms_mm * 1e3, 2), "torch_mm_GBps": round(gbs(ms_mm), 1),
+        "roofline": {"bound": "hbm", "achieved": round(gbs(ms_row), 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs(ms_row) / peaks["hbm_gbs"], 4),
+                     "traffic": read_traffic_per_launch("skinny_32768x1024x256")},
+    }
+    del sets, bcol
+    # --- 8192^3, uniform inputs, both layouts; two operand sets (> L2 together)
+    n = 8192
+    ops = [((torch.rand((n, n), generator=g, device=dev) * 2 - 1).half(),
+            (torch.rand((n, n), generator=g, device=dev) * 2 - 1).half()) for _ in range(2)]
+    opsc = [b.t().contiguous() for _, b in ops]
+    Cbuf = torch.empty((n, n), device=dev, dtype=torch.float16)
+    fl = 2.0 * n ** 3
+    res = {}
+    for name, f in (("rowB", lambda i: tg.gemm(ops[i % 2][0], ops[i % 2][1], out=Cbuf)),
+                    ("colb", lambda i: tg.gemm_pretransposed(ops[i % 2][0], opsc[i % 2],
+                                                             mode="reg_pingpong_256_colb")),
+                    ("torch_mm", lambda i: torch.mm(ops[i % 2][0], ops[i % 2][1], out=Cbuf))):
+        for i in range(4):
+            f(i)
+        ms = _time_launches(torch, f, 20)
+        res[name + "_TFLOPs"] = round(fl / (ms * 1e-3) / 1e12, 1)
+    res["rowB_frac_of_measured_bf16_burst"] = round(res["rowB_TFLOPs"] / peaks["bf16_tflops"], 4)
+    out["square_8192"] = res
+    return out
+
+
+def run_b200(args) -> int:
+    sys.path.insert(0, str(PKG_DIR))
+    import torch
+    import torch.distributed as dist
+
+    import tensorcore_gemm as tg
+    from tensorcore_gemm import _native, sharded
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    peaks, peaks_src = load_peaks()
+    _native.load()
+
+    lo, hi = sharded.row_shard_bounds(M_TOTAL, world, rank)
+    m = hi - lo
+    gA = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gB = torch.Generator(device=dev).manual_seed(1)
+    A = torch.randn((m, K_DIM), generator=gA, device=dev, dtype=torch.float16) * STD
+    B = torch.randn((K_DIM, N_DIM), generator=gB, device=dev, dtype=torch.float16) * STD
+    C = torch.empty((m, N_DIM), device=dev, dtype=torch.float16)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    step = lambda: sharded.sharded_gemm(A, B, out=C)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if _native.last_device_error() != 0:
+        raise RuntimeError("device error word set during warm-up")
+
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms_local)
+    dev_err = _native.last_device_error()
+    total_flops = 2.0 * M_TOTAL * N_DIM * K_DIM * args.steps
+    value = total_flops / (ms_max * 1e-3) / 1e12
+    launch_ms = ms_local / args.steps
+    achieved = 2.0 * m * N_DIM * K_DIM / (launch_ms * 1e-3) / 1e12
+    peak_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
+
+    # ---- end to end through the public API with host buffers
+    e2e_steps = max(1, min(args.steps, 5))
+    A_h = A.cpu().pin_memory()
+    B_h = B.cpu().pin_memory()
+    C_h = torch.empty((m, N_DIM), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        A.copy_(A_h, non_blocking=True)
+        B.copy_(B_h, non_blocking=True)
+        tg.gemm(A, B, out=C)
+        C_h.copy_(C, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    ev1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    e2e_value = 2.0 * M_TOTAL * N_DIM * K_DIM * e2e_steps / (e2e_ms * 1e-3) / 1e12
+
+    extras = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        del A_h, B_h, C_h
+        extras = side_measurements(torch, tg, dev, peaks)
+        cpu = CpuBaseline(target_s=3.0).measure(reps=3)
+
+    if rank == 0:
+        clk = clocks.summary()
+        line = {
+            "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 in / f32 accumulate / f16 out",
+            "data": "synthetic N(0,0.02) fp16, seeded on device", "config": workload_config(world),
+            "tflops_per_gpu": round(value / world, 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks[peak_key],
+                         "unit": "TFLOP/s", "frac": round(achieved / peaks[peak_key], 4),
+                         "peak_source": f"{peaks_src} {peak_key}",
+                         "traffic": read_traffic_per_launch(f"shard_{m}x{N_DIM}x{K_DIM}")},
+            "pct_nominal_dense_fp16_peak": round(100 * value / world / 2250.0, 2),
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(2 * (m * K_DIM + K_DIM * N_DIM)),
+                    "d2h_bytes_per_step": int(2 * m * N_DIM), "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "device_error_word": dev_err,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if extras is not None:
+            line["extras"] = extras
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

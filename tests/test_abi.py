@@ -1,0 +1,74 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and rejects
+bad arguments before touching the GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def _declared_symbols():
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        names += re.findall(r"B200_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+    return names
+
+
+def test_header_declares_entry_points():
+    names = _declared_symbols()
+    assert "b200_gemm_f16" in names and "b200_gemm_strerror" in names
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol(native_lib):
+    for name in _declared_symbols():
+        assert hasattr(native_lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_version_and_strerror(native_lib):
+    from tensorcore_gemm import _native
+
+    assert _native.version() >= 100
+    for code in range(0, 8):
+        assert _native.strerror(code)
+    assert "unknown" in _native.strerror(999)
+
+
+@pytest.mark.parametrize("args,code", [
+    # (M, N, K, lda, ldb, ldc, layout)
+    ((-1, 8, 8, 8, 8, 8, 0), 1),
+    ((8, -1, 8, 8, 8, 8, 0), 1),
+    ((8, 8, -1, 8, 8, 8, 0), 1),
+    ((8, 8, 8, 8, 8, 8, 2), 1),
+    ((1 << 31, 8, 8, 8, 8, 8, 0), 3),
+    ((0, 8, 8, 8, 8, 8, 0), 0),   # empty output: nothing to do
+    ((8, 0, 8, 8, 8, 8, 1), 0),
+])
+def test_argument_validation_without_gpu(native_lib, args, code):
+    from tensorcore_gemm import _native
+
+    M, N, K, lda, ldb, ldc, layout = args
+    got = _native.gemm_f16_raw(0, 0, 0, M, N, K, lda, ldb, ldc, layout, 0)
+    assert got == code
+
+
+def test_null_output_rejected(native_lib):
+    from tensorcore_gemm import _native
+
+    assert _native.gemm_f16_raw(16, 16, 0, 8, 8, 8, 8, 8, 8, 0, 0) == _native.B200_ERR_INVALID_ARGUMENT
+
+
+def test_misaligned_output_rejected(native_lib):
+    from tensorcore_gemm import _native
+
+    buf = ctypes.create_string_buffer(4096)
+    base = (ctypes.addressof(buf) + 15) & ~15
+    assert _native.gemm_f16_raw(base, base, base + 2, 8, 8, 8, 8, 8, 8, 0, 0) == _native.B200_ERR_MISALIGNED
+    assert _native.gemm_f16_raw(base, base, base, 8, 8, 8, 8, 8, 12, 0, 0) == _native.B200_ERR_MISALIGNED
+    assert _native.gemm_f16_raw(base, base, base, 8, 12, 8, 8, 8, 8, 0, 0) == _native.B200_ERR_INVALID_ARGUMENT

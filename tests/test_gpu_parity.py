@@ -1,0 +1,171 @@
+"""GPU parity of the B200 kernels through the public API and the C ABI.
+
+Bar (north star): max|C - C_ref| <= 2e-3 * sqrt(K) * RMS(C_ref), C_ref the fp32
+product of the same fp16 inputs; small cases are also checked against the C
+oracle and the committed golden vectors of the reference's output.
+"""
+from __future__ import annotations
+
+import importlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import tensorcore_gemm as tg
+from gpu_util import assert_parity, fp32_ref, oracle_check
+from oracle import oracle
+from tensorcore_gemm import _native
+
+pytestmark = pytest.mark.gpu
+gemm_mod = importlib.import_module("tensorcore_gemm.gemm")
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _inputs(M, N, K, dev, dist="uniform", seed=0, std=1.0):
+    A, B = oracle.make_inputs(M, N, K, dist=dist, seed_a=seed, seed_b=seed + 1, std=std)
+    return A.to(dev), B.to(dev)
+
+
+def _no_device_error():
+    assert _native.last_device_error() == 0
+
+
+def test_golden_vectors_on_gpu(cuda_device, native_lib):
+    meta = json.loads((GOLDEN / "gemm_golden.json").read_text())
+    data = np.load(GOLDEN / "gemm_golden.npz")
+    for c in meta["cases"]:
+        n = c["name"]
+        A = torch.from_numpy(data[n + "__A"]).to(cuda_device)
+        B = torch.from_numpy(data[n + "__B"]).to(cuda_device)
+        C_ref = data[n + "__C"].astype(np.float32)
+        for C in (tg.gemm(A, B), tg.gemm_pretransposed(A, B.t().contiguous(), mode="reg_pingpong_256_colb")):
+            got = C.float().cpu().numpy()
+            assert_parity(C, fp32_ref(A, B), c["K"], n)
+            ulp = np.abs(np.spacing(data[n + "__C"])).astype(np.float32).max()
+            assert np.abs(got - C_ref).max() <= 2 * ulp, f"{n}: differs from the reference output by > 2 ulp"
+    _no_device_error()
+
+
+SMALL = [(1, 8, 8), (8, 8, 8), (37, 24, 40), (128, 256, 64), (129, 264, 72), (255, 136, 200),
+         (64, 1024, 16), (300, 8, 1000), (1000, 1000, 1000), (513, 520, 8)]
+
+
+@pytest.mark.parametrize("M,N,K", SMALL)
+@pytest.mark.parametrize("colb", [False, True])
+def test_small_shapes_vs_oracle(cuda_device, native_lib, M, N, K, colb):
+    A, B = _inputs(M, N, K, cuda_device, seed=M + N + K)
+    if colb:
+        C = tg.gemm_pretransposed(A, B.t().contiguous(), mode="reg_pingpong_256_colb_mma")
+    else:
+        C = tg.gemm(A, B, mode="reg_pingpong_256_mma")
+    torch.cuda.synchronize()
+    oracle_check(C, A, B)
+    _no_device_error()
+
+
+BASELINE_SHAPES = [
+    (2048, 2048, 2048, "uniform"),
+    (16384, 256, 256, "normal"), (16384, 512, 256, "normal"), (16384, 1024, 256, "normal"),
+    (32768, 256, 256, "normal"), (32768, 512, 256, "normal"), (32768, 1024, 256, "normal"),
+    (4096, 4096, 4096, "uniform"), (8192, 8192, 8192, "uniform"),
+    (4096, 8192, 4096, "uniform"), (8192, 4096, 4096, "uniform"), (4000, 6000, 3000, "uniform"),
+]
+
+
+@pytest.mark.parametrize("M,N,K,dist", BASELINE_SHAPES)
+def test_baseline_configs(cuda_device, native_lib, M, N, K, dist):
+    A, B = _inputs(M, N, K, cuda_device, dist=dist)
+    ref = fp32_ref(A, B)
+    assert_parity(tg.gemm(A, B, mode="reg_pingpong_256"), ref, K, f"{M}x{N}x{K} rowB")
+    Bc = B.t().contiguous()
+    assert_parity(tg.gemm_pretransposed(A, Bc, mode="reg_pingpong_256_colb"), ref, K, f"{M}x{N}x{K} colb")
+    _no_device_error()
+
+
+def test_multi_gpu_shard_shape(cuda_device, native_lib):
+    # One rank's shard of the 65536 x 8192 x 8192 config at 8 GPUs (8192 rows),
+    # N(0, 0.02) operands.
+    A, B = _inputs(8192, 8192, 8192, cuda_device, dist="normal", std=0.02)
+    assert_parity(tg.gemm(A, B), fp32_ref(A, B), 8192, "shard")
+    _no_device_error()
+
+
+def test_all_modes_agree(cuda_device, native_lib):
+    A, B = _inputs(384, 264, 320, cuda_device)
+    Bc = B.t().contiguous()
+    outs = [tg.gemm(A, B, mode=m) for m in tg.KERNEL_MODES]
+    outs += [tg.gemm_pretransposed(A, Bc, mode=m) for m in ("wmma", "mma", "reg_pingpong_256_colb",
+                                                            "reg_pingpong_256_colb_mma")]
+    # Reference quirk: ids 2/3 read the pretransposed operand as K x N.
+    outs += [tg.gemm_pretransposed(A, B, mode=m) for m in ("reg_pingpong_256", "reg_pingpong_256_mma")]
+    outs += [gemm_mod.root_gemm_cuda(A, B, 2), gemm_mod.root_gemm_cuda(A, Bc, 4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert_parity(outs[0], fp32_ref(A, B), 320)
+
+
+def test_deterministic(cuda_device, native_lib):
+    A, B = _inputs(2048, 2048, 2048, cuda_device)
+    C1 = tg.gemm(A, B)
+    C2 = tg.gemm(A, B)
+    assert torch.equal(C1, C2)
+
+
+def test_k_zero_gives_zeros(cuda_device, native_lib):
+    A = torch.empty((64, 0), dtype=torch.float16, device=cuda_device)
+    B = torch.empty((0, 72), dtype=torch.float16, device=cuda_device)
+    C = tg.gemm(A, B)
+    assert C.shape == (64, 72) and not C.any()
+
+
+def test_empty_output(cuda_device, native_lib):
+    A = torch.ones((0, 64), dtype=torch.float16, device=cuda_device)
+    B = torch.ones((64, 16), dtype=torch.float16, device=cuda_device)
+    assert tg.gemm(A, B).shape == (0, 16)
+
+
+def test_output_guard_bands_untouched(cuda_device, native_lib):
+    """Canary: a C view inside a larger buffer; nothing outside it is written."""
+    M, N, K = 200, 136, 96
+    A, B = _inputs(M, N, K, cuda_device)
+    ld = 256
+    buf = torch.full((M + 64, ld), 7.0, dtype=torch.float16, device=cuda_device)
+    view = buf[32:32 + M, 64:64 + N]
+    code = _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), view.data_ptr(), M, N, K, K, N, ld,
+                                _native.B200_B_ROW_MAJOR, torch.cuda.current_stream().cuda_stream)
+    assert code == 0
+    torch.cuda.synchronize()
+    assert_parity(view, fp32_ref(A, B), K)
+    mask = torch.ones_like(buf, dtype=torch.bool)
+    mask[32:32 + M, 64:64 + N] = False
+    assert (buf[mask] == 7.0).all(), "kernel wrote outside the output view"
+
+
+def test_strided_views_without_copies(cuda_device, native_lib):
+    """Row-strided A, and B given as a transposed view, run in place."""
+    big = torch.randn((300, 512), device=cuda_device).half()
+    A = big[:, 64:64 + 256]                    # lda = 512
+    Bt = torch.randn((200, 256), device=cuda_device).half()
+    B = Bt.t()                                 # K x N view of an N x K buffer
+    C = tg.gemm(A, B)
+    assert_parity(C, A.float() @ B.float(), 256)
+
+
+def test_unsupported_alignment_raises(cuda_device, native_lib):
+    A = torch.ones((16, 12), dtype=torch.float16, device=cuda_device)
+    B = torch.ones((12, 16), dtype=torch.float16, device=cuda_device)
+    assert not tg.is_supported(A, B)
+    with pytest.raises(RuntimeError):
+        tg.gemm(A, B)
+
+
+def test_current_stream_is_used(cuda_device, native_lib):
+    A, B = _inputs(512, 512, 512, cuda_device)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        C = tg.gemm(A, B)
+    s.synchronize()
+    assert_parity(C, fp32_ref(A, B), 512)

@@ -1,0 +1,66 @@
+"""CPU: row-shard bookkeeping and the C all-gather with two gloo ranks."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tensorcore_gemm import sharded
+
+
+@pytest.mark.parametrize("M,world", [(65536, 1), (65536, 2), (65536, 8), (1000, 3), (5, 4), (0, 2), (129, 2)])
+def test_shards_cover_rows_exactly_once(M, world):
+    b = sharded.all_shard_bounds(M, world)
+    assert b[0][0] == 0 and b[-1][1] == M
+    for (a0, a1), (b0, b1) in zip(b, b[1:]):
+        assert a1 == b0 and a0 <= a1
+    for lo, _ in b:
+        assert lo % sharded.SHARD_ALIGN_ROWS == 0 or lo == M
+
+
+def test_even_split_of_config_shape():
+    assert sharded.all_shard_bounds(65536, 8) == [(r * 8192, (r + 1) * 8192) for r in range(8)]
+
+
+def test_bad_rank():
+    with pytest.raises(ValueError):
+        sharded.row_shard_bounds(10, 2, 2)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, M, N, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lo, hi = sharded.row_shard_bounds(M, world, rank)
+        # Stand-in for this rank's GEMM output: row index encoded in the values.
+        shard = torch.arange(lo, hi, dtype=torch.float32).unsqueeze(1).repeat(1, N).half()
+        full = sharded.all_gather_rows(shard, M)
+        want = torch.arange(M, dtype=torch.float32).unsqueeze(1).repeat(1, N).half()
+        q.put((rank, bool(torch.equal(full, want))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M", [512, 300])
+def test_all_gather_two_gloo_ranks(M):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, M, 8, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    results = dict(q.get(timeout=10) for _ in procs)
+    assert all(p.exitcode == 0 for p in procs)
+    assert results == {0: True, 1: True}
