@@ -1,0 +1,243 @@
+// 2-CTA (cta_group::2) tcgen05 GEMM kernel: a cluster of two CTAs on two SMs
+// computes one 256 x 256 output tile with M=256, N=256 MMAs.
+//
+//   * CTA r of the pair loads A rows [m0 + 128 r, +128) and B columns
+//     [n0 + 128 r, +128) into its own shared memory (plain TMA, no multicast);
+//     the loads of both CTAs complete on the leader's (r = 0) full barrier.
+//   * The leader's MMA lane issues tcgen05.mma.cta_group::2, which reads A and
+//     B halves from both CTAs and writes rows [128 r, +128) of the fp32 tile
+//     into CTA r's TMEM.
+//   * The leader frees a stage / publishes an accumulator with one
+//     tcgen05.commit per CTA (own barrier, then the peer's through mapa).
+//   * Each CTA's epilogue stores its own 128 rows; the peer's epilogue warps
+//     release the accumulator with a remote arrive on the leader's barrier.
+// Per SM this halves the B bytes staged per FLOP compared with the 1-CTA
+// 128 x 256 tile.
+#pragma once
+
+#include "gemm_common.cuh"
+
+namespace b200 {
+
+template <int STAGES>
+struct PairConfig {
+  static constexpr int kTileM = 256;                 // rows per pair tile
+  static constexpr int kTileN = 256;                 // columns per pair tile
+  static constexpr int kHalfN = 128;                 // B columns staged per CTA
+  static constexpr int kABytes = kBM * kBK * 2;      // 16 KB
+  static constexpr int kBBytes = kHalfN * kBK * 2;   // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int kTmemCols = 2 * kTileN;       // two 256-column accumulators
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 256 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
+};
+
+template <int STAGES, bool kBRowMajor>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                 const __grid_constant__ CUtensorMap tmap_b,
+                                 const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m) {
+  using Cfg = PairConfig<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * Cfg::kABytes;
+  uint8_t* smem_epi = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
+  uint64_t* full_bar = bars;                     // [STAGES] leader: both CTAs' loads landed
+  uint64_t* empty_bar = bars + STAGES;           // [STAGES] each CTA: its stage may be refilled
+  uint64_t* tmem_full = bars + 2 * STAGES;       // [2]      each CTA: accumulator ready
+  uint64_t* tmem_empty = bars + 2 * STAGES + 2;  // [2]      leader: both epilogues done reading
+  uint64_t* mma_drain = bars + 2 * STAGES + 4;   // [1]      abort path only
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  TileScheduler sched;
+  sched.num_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
+  sched.num_n = (N + Cfg::kTileN - 1) / Cfg::kTileN;
+  sched.group_m = group_m;
+  const int num_tiles = sched.num_m * sched.num_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_c);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 2 * kEpiWarps);
+    }
+    mbar_init(mma_drain, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(tmem_base_slot, Cfg::kTmemCols);
+    tmem_relinquish_alloc_permit<2>();
+  }
+  tc_fence_before_sync();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (one lane per CTA) ----------------
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_normal();
+      const uint64_t pol_b = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        sched.tile_coords(t, mb, nb);
+        const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * kBM;
+        const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kStageBytes);
+          const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          const int k0 = kb * kBK;
+          tma_load_2d_pair(smem_a + stage * Cfg::kABytes, &tmap_a, full_leader, k0, m0, pol_a);
+          uint8_t* b_dst = smem_b + stage * Cfg::kBBytes;
+          if constexpr (kBRowMajor) {
+#pragma unroll
+            for (int p = 0; p < Cfg::kHalfN / 64; ++p)
+              tma_load_2d_pair(b_dst + p * (kBK * 128), &tmap_b, full_leader, nh0 + 64 * p, k0, pol_b);
+          } else {
+            tma_load_2d_pair(b_dst, &tmap_b, full_leader, k0, nh0, pol_b);
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok && leader) {
+        const uint32_t pending = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (uint32_t i = 0; i < pending; ++i) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(&full_bar[s], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA, one lane) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc =
+          make_idesc_f16_f32(Cfg::kTileM, Cfg::kTileN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
+      const uint32_t a_base = smem_u32(smem_a);
+      const uint32_t b_base = smem_u32(smem_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      bool any_mma = false;
+      int local = 0;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint32_t a_addr = a_base + stage * Cfg::kABytes;
+          const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
+            uint64_t bdesc;
+            if constexpr (kBRowMajor)
+              bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), kBK * 128);
+            else
+              bdesc = make_desc_kmajor_sw128(b_addr + k * (kUmmaK * 2));
+            umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          any_mma = true;
+          const uint32_t e = smem_u32(&empty_bar[stage]);
+          umma_commit_cta2(e);
+          umma_commit_cta2(mapa_shared(e, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&tmem_full[acc]);
+        umma_commit_cta2(f);
+        umma_commit_cta2(mapa_shared(f, 1));
+      }
+      if (!ok && any_mma) {
+        umma_commit_cta2(smem_u32(mma_drain));
+        mbar_wait_drain(mma_drain, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 (both CTAs) ----------------
+    const int quad = warp & 3;
+    const int ew = warp - 2;
+    uint8_t* epi_buf = smem_epi + ew * 2 * kEpiBufBytes;
+    const uint32_t epi_addr = smem_u32(epi_buf);
+    int buf = 0;
+    int local = 0;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++local) {
+      int mb, nb;
+      sched.tile_coords(t, mb, nb);
+      const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * kBM;
+      const int n0 = nb * Cfg::kTileN;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue)) break;
+      tc_fence_after_sync();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * Cfg::kTileN;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+        uint32_t lo[32], hi[32];
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
+        tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
+        tmem_ld_wait_regs(lo);
+        tmem_ld_wait_regs(hi);
+        if (c == Cfg::kTileN / kEpiCols - 1) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
+        }
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = epi_addr + buf * kEpiBufBytes + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
+          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
+                       pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_c, epi_buf + buf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
+          bulk_commit_group();
+        }
+        buf ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before_sync();
+  cluster_sync();  // no CTA leaves while its peer may still signal it or read its smem
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc<2>(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace b200

@@ -48,6 +48,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 side measurements")
+    ap.add_argument("--case", default=None,
+                    help="single-GEMM mode for profiling/tuning: MxNxK[:colb] (1 GPU, not the driver line)")
+    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "torch"],
+                    help="kernel for --case (torch = torch.mm comparator)")
+    ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"], help="inputs for --case")
     return ap.parse_args()
 
 
@@ -456,8 +461,58 @@ def run_b200(args) -> int:
     return 0
 
 
+def run_case(args) -> int:
+    """One GEMM shape: W warm-up + K timed launches over rotating operand sets
+    (at least 2x L2 in total, so every launch streams from HBM); one JSON line."""
+    sys.path.insert(0, str(PKG_DIR))
+    import torch
+
+    import tensorcore_gemm as tg
+    from tensorcore_gemm import _native
+
+    shape, _, layout = args.case.partition(":")
+    M, N, K = (int(x) for x in shape.lower().split("x"))
+    colb = layout == "colb"
+    dev = torch.device("cuda", 0)
+    if args.variant != "torch":
+        _native.set_variant(args.variant)
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    set_bytes = 2 * (M * K + K * N + M * N)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nsets = max(1, min(8, -(-2 * l2 // set_bytes)))
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def mk(r, c):
+        if args.dist == "uniform":
+            return (torch.rand((r, c), generator=g, device=dev) * 2 - 1).half()
+        return torch.randn((r, c), generator=g, device=dev, dtype=torch.float16)
+
+    sets = [(mk(M, K), mk(N, K) if colb else mk(K, N), torch.empty((M, N), device=dev, dtype=torch.float16))
+            for _ in range(nsets)]
+
+    def f(i):
+        A, B, C = sets[i % nsets]
+        if args.variant == "torch":
+            return torch.mm(A, B.t() if colb else B, out=C)
+        if colb:
+            return tg.gemm_pretransposed(A, B, mode="reg_pingpong_256_colb")
+        return tg.gemm(A, B, out=C)
+
+    for i in range(max(args.warmup, 1)):
+        f(i)
+    ms = _time_launches(torch, f, args.steps)
+    err = _native.last_device_error()
+    print(json.dumps({"case": args.case, "variant": args.variant, "dist": args.dist, "us": round(ms * 1e3, 2),
+                      "TFLOPs": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
+                      "GBps": round(set_bytes / (ms * 1e-3) / 1e9, 1), "operand_sets": nsets,
+                      "device_error_word": err}), flush=True)
+    return 0 if err == 0 else 1
+
+
 def main() -> int:
     args = parse_args()
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -71,6 +71,18 @@ B200_API int b200_gemm_last_device_error(void);
  * (0 on error).  No counterpart in the reference. */
 B200_API int b200_gemm_sm_count(void);
 
+/* Kernel variants for b200_gemm_set_variant. */
+#define B200_VARIANT_AUTO 0 /* shape heuristic (default) */
+#define B200_VARIANT_CTA1 1 /* 1-CTA persistent kernel, 128 x 256 tiles */
+#define B200_VARIANT_PAIR 2 /* 2-CTA cluster (cta_group::2) kernel, 256 x 256 tiles */
+
+/* Process-wide override of the kernel the library picks, for tests and
+ * tuning; every variant computes the same product.  Returns
+ * B200_ERR_INVALID_ARGUMENT for an unknown variant.  No counterpart in the
+ * reference (its mode string chose among kernels; here the mode only selects
+ * the B layout). */
+B200_API int b200_gemm_set_variant(int variant);
+
 /* Library ABI version (major * 100 + minor). */
 B200_API int b200_gemm_version(void);
 

@@ -72,3 +72,12 @@ def test_misaligned_output_rejected(native_lib):
     assert _native.gemm_f16_raw(base, base, base + 2, 8, 8, 8, 8, 8, 8, 0, 0) == _native.B200_ERR_MISALIGNED
     assert _native.gemm_f16_raw(base, base, base, 8, 8, 8, 8, 8, 12, 0, 0) == _native.B200_ERR_MISALIGNED
     assert _native.gemm_f16_raw(base, base, base, 8, 12, 8, 8, 8, 8, 0, 0) == _native.B200_ERR_INVALID_ARGUMENT
+
+
+def test_set_variant_validation(native_lib):
+    from tensorcore_gemm import _native
+
+    assert native_lib.b200_gemm_set_variant(99) == _native.B200_ERR_INVALID_ARGUMENT
+    assert native_lib.b200_gemm_set_variant(-1) == _native.B200_ERR_INVALID_ARGUMENT
+    for v in ("pair", "cta1", "auto"):
+        _native.set_variant(v)

@@ -29,11 +29,18 @@ def _inputs(M, N, K, dev, dist="uniform", seed=0, std=1.0):
     return A.to(dev), B.to(dev)
 
 
+@pytest.fixture(params=["auto", "cta1", "pair"])
+def variant(request, native_lib):
+    _native.set_variant(request.param)
+    yield request.param
+    _native.set_variant("auto")
+
+
 def _no_device_error():
     assert _native.last_device_error() == 0
 
 
-def test_golden_vectors_on_gpu(cuda_device, native_lib):
+def test_golden_vectors_on_gpu(cuda_device, variant):
     meta = json.loads((GOLDEN / "gemm_golden.json").read_text())
     data = np.load(GOLDEN / "gemm_golden.npz")
     for c in meta["cases"]:
@@ -55,7 +62,7 @@ SMALL = [(1, 8, 8), (8, 8, 8), (37, 24, 40), (128, 256, 64), (129, 264, 72), (25
 
 @pytest.mark.parametrize("M,N,K", SMALL)
 @pytest.mark.parametrize("colb", [False, True])
-def test_small_shapes_vs_oracle(cuda_device, native_lib, M, N, K, colb):
+def test_small_shapes_vs_oracle(cuda_device, variant, M, N, K, colb):
     A, B = _inputs(M, N, K, cuda_device, seed=M + N + K)
     if colb:
         C = tg.gemm_pretransposed(A, B.t().contiguous(), mode="reg_pingpong_256_colb_mma")
@@ -76,7 +83,7 @@ BASELINE_SHAPES = [
 
 
 @pytest.mark.parametrize("M,N,K,dist", BASELINE_SHAPES)
-def test_baseline_configs(cuda_device, native_lib, M, N, K, dist):
+def test_baseline_configs(cuda_device, variant, M, N, K, dist):
     A, B = _inputs(M, N, K, cuda_device, dist=dist)
     ref = fp32_ref(A, B)
     assert_parity(tg.gemm(A, B, mode="reg_pingpong_256"), ref, K, f"{M}x{N}x{K} rowB")
@@ -93,7 +100,7 @@ def test_multi_gpu_shard_shape(cuda_device, native_lib):
     _no_device_error()
 
 
-def test_all_modes_agree(cuda_device, native_lib):
+def test_all_modes_agree(cuda_device, variant):
     A, B = _inputs(384, 264, 320, cuda_device)
     Bc = B.t().contiguous()
     outs = [tg.gemm(A, B, mode=m) for m in tg.KERNEL_MODES]
@@ -127,7 +134,7 @@ def test_empty_output(cuda_device, native_lib):
     assert tg.gemm(A, B).shape == (0, 16)
 
 
-def test_output_guard_bands_untouched(cuda_device, native_lib):
+def test_output_guard_bands_untouched(cuda_device, variant):
     """Canary: a C view inside a larger buffer; nothing outside it is written."""
     M, N, K = 200, 136, 96
     A, B = _inputs(M, N, K, cuda_device)
@@ -144,7 +151,7 @@ def test_output_guard_bands_untouched(cuda_device, native_lib):
     assert (buf[mask] == 7.0).all(), "kernel wrote outside the output view"
 
 
-def test_strided_views_without_copies(cuda_device, native_lib):
+def test_strided_views_without_copies(cuda_device, variant):
     """Row-strided A, and B given as a transposed view, run in place."""
     big = torch.randn((300, 512), device=cuda_device).half()
     A = big[:, 64:64 + 256]                    # lda = 512
@@ -169,3 +176,17 @@ def test_current_stream_is_used(cuda_device, native_lib):
         C = tg.gemm(A, B)
     s.synchronize()
     assert_parity(C, fp32_ref(A, B), 512)
+
+
+def test_variants_deterministic_and_within_bound(cuda_device, native_lib):
+    A, B = _inputs(1024, 1536, 2048, cuda_device)
+    ref = fp32_ref(A, B)
+    for v in ("cta1", "pair"):
+        _native.set_variant(v)
+        try:
+            C1 = tg.gemm(A, B)
+            C2 = tg.gemm(A, B)
+        finally:
+            _native.set_variant("auto")
+        assert torch.equal(C1, C2)
+        assert_parity(C1, ref, 2048, v)
