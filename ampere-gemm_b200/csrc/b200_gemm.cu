@@ -152,21 +152,21 @@ int max_active_pairs(Kern kern, int smem_bytes, int sm_count) {
   return n;
 }
 
-template <int STAGES, bool kBRowMajor>
+template <int STAGES, int KSUB, bool kBRowMajor>
 int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
                         int64_t ldc, int sm_count, int group_m, cudaStream_t stream) {
-  using Cfg = PairConfig<STAGES>;
+  using Cfg = PairConfig<STAGES, KSUB>;
   CUtensorMap ta, tb, tc;
   int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   if (kBRowMajor)
-    rc = make_tmap_2d(&tb, B, K, N, ldb, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    rc = make_tmap_2d(&tb, B, K, N, ldb, 64, Cfg::kStageK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   else
     rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, Cfg::kHalfN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, kBRowMajor>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, kBRowMajor>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess)
     return B200_ERR_CUDA;
   static int pairs_cache[kMaxDevices] = {0};
@@ -239,11 +239,11 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
   }
   const int gm = group_m_override();
   if (variant == B200_VARIANT_PAIR) {
-    const int group_m = gm ? gm : 8;
-    if (row_b) return launch_tcgen05_pair<6, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
-    return launch_tcgen05_pair<6, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    const int group_m = gm ? gm : 16;  // 16 x 256-row bands: best measured on 8192^3 and 65536 x 8192^2
+    if (row_b) return launch_tcgen05_pair<3, 2, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    return launch_tcgen05_pair<3, 2, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
   }
-  const int group_m = gm ? gm : 8;
+  const int group_m = gm ? gm : 16;
   if (row_b)
     return launch_tcgen05<256, 4, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
   return launch_tcgen05<256, 4, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
@@ -285,3 +285,14 @@ extern "C" int b200_gemm_sm_count(void) {
 }
 
 extern "C" int b200_gemm_version(void) { return 100; }
+
+#ifdef B200_GEMM_PROFILE
+// Copies and clears the per-CTA wait counters (profiling builds only).
+extern "C" __attribute__((visibility("default"))) int b200_gemm_debug_read_profile(unsigned long long* host, int rows) {
+  if (rows > 1024) rows = 1024;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(host, b200::g_prof, sizeof(unsigned long long) * 8 * rows) != cudaSuccess) return -1;
+  static unsigned long long zeros[1024][8];
+  return cudaMemcpyToSymbol(b200::g_prof, zeros, sizeof(zeros)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -9,6 +9,32 @@
 
 namespace b200 {
 
+// Optional wait-time instrumentation (compile with -DB200_GEMM_PROFILE): per
+// CTA, cycles each role spends blocked on each barrier.  Off in the product.
+#ifdef B200_GEMM_PROFILE
+__device__ unsigned long long g_prof[1024][8];
+// Per-thread accumulators live in registers; flushed once at kernel end.
+#define B200_PROF_DECL unsigned long long prof_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define B200_TIMED(slot, expr)                   \
+  ({                                             \
+    const long long _t0 = clock64();             \
+    const bool _r = (expr);                      \
+    prof_acc[slot] += (unsigned long long)(clock64() - _t0); \
+    _r;                                          \
+  })
+#define B200_PROF_ADD(slot, v) (prof_acc[slot] += (unsigned long long)(v))
+#define B200_PROF_FLUSH                                                         \
+  if (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64) {             \
+    for (int _i = 0; _i < 8; ++_i)                                              \
+      if (prof_acc[_i]) atomicAdd(&g_prof[blockIdx.x & 1023][_i], prof_acc[_i]); \
+  }
+#else
+#define B200_PROF_DECL
+#define B200_TIMED(slot, expr) (expr)
+#define B200_PROF_ADD(slot, v) ((void)0)
+#define B200_PROF_FLUSH
+#endif
+
 constexpr int kBM = 128;         // rows of A / C per tile (one TMEM lane per row)
 constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of fp16
 constexpr int kUmmaK = 16;       // K per tcgen05.mma kind::f16

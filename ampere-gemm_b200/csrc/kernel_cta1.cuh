@@ -23,6 +23,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_drain = bars + 2 * STAGES + 4;  // [1]       abort path only
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
 
+  B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -71,7 +72,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         sched.tile_coords(t, mb, nb);
         const int m0 = mb * kBM, n0 = nb * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer)) { ok = false; break; }
+          if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
+#ifdef B200_GEMM_NOLOAD
+          mbar_arrive(&full_bar[stage]);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          continue;
+#endif
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
           const int k0 = kb * kBK;
           tma_load_2d(smem_a + stage * Cfg::kABytes, &tmap_a, &full_bar[stage], k0, m0, pol_a);
@@ -112,14 +119,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool any_mma = false;
       int local = 0;
+#ifdef B200_GEMM_PROFILE
+      const long long prof_t0 = clock64();
+#endif
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma)) { ok = false; break; }
+        if (!B200_TIMED(1, mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma))) { ok = false; break; }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma)) { ok = false; break; }
+          if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
@@ -131,7 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), kBK * 128);
             else
               bdesc = make_desc_kmajor_sw128(b_addr + k * (kUmmaK * 2));
+#ifndef B200_GEMM_NOMMA
             umma_f16_cta1(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+#endif
           }
           any_mma = true;
           umma_commit_cta1(&empty_bar[stage]);  // frees the stage once these MMAs have read it
@@ -140,6 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         umma_commit_cta1(&tmem_full[acc]);       // accumulator ready for the epilogue
       }
+      B200_PROF_ADD(4, clock64() - prof_t0);
       if (!ok && any_mma) {
         umma_commit_cta1(mma_drain);
         mbar_wait_drain(mma_drain, 0);
@@ -159,9 +172,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = mb * kBM, n0 = nb * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue)) break;
+      // One lane per warp polls; the other 31 park at __syncwarp instead of
+      // hammering the barrier word in shared memory beside the tensor core.
+      bool got = true;
+      if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue));
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
       tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+#ifdef B200_GEMM_NOEPI
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (false) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
+        else mbar_arrive(&tmem_empty[acc]);
+      }
+      continue;
+#endif
 #pragma unroll 1
       for (int c = 0; c < BN / kEpiCols; ++c) {
         uint32_t lo[32], hi[32];
@@ -200,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) bulk_wait_group<0>();
   }
 
+  B200_PROF_FLUSH
   tc_fence_before_sync();
   __syncthreads();
   if (warp == 1) {

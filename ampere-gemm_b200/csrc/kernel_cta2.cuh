@@ -12,20 +12,26 @@
 //   * Each CTA's epilogue stores its own 128 rows; the peer's epilogue warps
 //     release the accumulator with a remote arrive on the leader's barrier.
 // Per SM this halves the B bytes staged per FLOP compared with the 1-CTA
-// 128 x 256 tile.
+// 128 x 256 tile.  A stage holds KSUB 64-wide K slices: commits of a pair
+// reach their barriers late (about 1.6k cycles after issue), so a stage of
+// 8 MMAs (KSUB = 2) keeps the tensor pipe fed where 4 per stage does not.
 #pragma once
 
 #include "gemm_common.cuh"
 
 namespace b200 {
 
-template <int STAGES>
+template <int STAGES, int KSUB>
 struct PairConfig {
+  static constexpr int kStageK = kBK * KSUB;         // K per stage (KSUB swizzle atoms)
   static constexpr int kTileM = 256;                 // rows per pair tile
   static constexpr int kTileN = 256;                 // columns per pair tile
   static constexpr int kHalfN = 128;                 // B columns staged per CTA
-  static constexpr int kABytes = kBM * kBK * 2;      // 16 KB
-  static constexpr int kBBytes = kHalfN * kBK * 2;   // 16 KB
+  static constexpr int kASub = kBM * kBK * 2;       // 16 KB per 64-wide K slice of A
+  static constexpr int kBSub = kHalfN * kBK * 2;     // 16 KB per 64-wide K slice of B (col-major B)
+  static constexpr int kABytes = kASub * KSUB;
+  static constexpr int kBBytes = kBSub * KSUB;
+  static constexpr int kBPanel = kStageK * 128;      // row-major B: one 64-column panel of kStageK rows
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
   static constexpr int kTmemCols = 2 * kTileN;       // two 256-column accumulators
@@ -33,12 +39,12 @@ struct PairConfig {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int STAGES, bool kBRowMajor>
+template <int STAGES, int KSUB, bool kBRowMajor>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m) {
-  using Cfg = PairConfig<STAGES>;
+  using Cfg = PairConfig<STAGES, KSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
@@ -52,6 +58,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* mma_drain = bars + 2 * STAGES + 4;   // [1]      abort path only
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
 
+  B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -64,7 +71,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   sched.num_n = (N + Cfg::kTileN - 1) / Cfg::kTileN;
   sched.group_m = group_m;
   const int num_tiles = sched.num_m * sched.num_n;
-  const int num_kb = (K + kBK - 1) / kBK;
+  const int num_kb = (K + Cfg::kStageK - 1) / Cfg::kStageK;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmap_a);
@@ -105,18 +112,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * kBM;
         const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer)) { ok = false; break; }
+          if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
+#ifdef B200_GEMM_NOLOAD
+          if (leader) mbar_arrive(&full_bar[stage]);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          continue;
+#endif
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kStageBytes);
           const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          const int k0 = kb * kBK;
-          tma_load_2d_pair(smem_a + stage * Cfg::kABytes, &tmap_a, full_leader, k0, m0, pol_a);
+          const int k0 = kb * Cfg::kStageK;
           uint8_t* b_dst = smem_b + stage * Cfg::kBBytes;
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub)
+            tma_load_2d_pair(smem_a + stage * Cfg::kABytes + sub * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
+                             m0, pol_a);
           if constexpr (kBRowMajor) {
+            // Panels of 64 columns x kStageK rows (one box each).
 #pragma unroll
             for (int p = 0; p < Cfg::kHalfN / 64; ++p)
-              tma_load_2d_pair(b_dst + p * (kBK * 128), &tmap_b, full_leader, nh0 + 64 * p, k0, pol_b);
+              tma_load_2d_pair(b_dst + p * Cfg::kBPanel, &tmap_b, full_leader, nh0 + 64 * p, k0, pol_b);
           } else {
-            tma_load_2d_pair(b_dst, &tmap_b, full_leader, k0, nh0, pol_b);
+#pragma unroll
+            for (int sub = 0; sub < KSUB; ++sub)
+              tma_load_2d_pair(b_dst + sub * Cfg::kBSub, &tmap_b, full_leader, k0 + kBK * sub, nh0, pol_b);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -144,26 +163,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool any_mma = false;
       int local = 0;
+#ifdef B200_GEMM_PROFILE
+      const long long prof_t0 = clock64();
+#endif
       for (int t = pair; t < num_tiles && ok; t += num_pairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma)) { ok = false; break; }
+        if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma))) { ok = false; break; }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma)) { ok = false; break; }
+          if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
+          for (int k = 0; k < Cfg::kStageK / kUmmaK; ++k) {
+            const int sub = k / (kBK / kUmmaK), j = k % (kBK / kUmmaK);
+            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + sub * Cfg::kASub + j * (kUmmaK * 2));
             uint64_t bdesc;
             if constexpr (kBRowMajor)
-              bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), kBK * 128);
+              bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), Cfg::kBPanel);
             else
-              bdesc = make_desc_kmajor_sw128(b_addr + k * (kUmmaK * 2));
+              bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
+#ifndef B200_GEMM_NOMMA
             umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+#endif
           }
           any_mma = true;
           const uint32_t e = smem_u32(&empty_bar[stage]);
@@ -176,6 +201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         umma_commit_cta2(f);
         umma_commit_cta2(mapa_shared(f, 1));
       }
+      B200_PROF_ADD(4, clock64() - prof_t0);
       if (!ok && any_mma) {
         umma_commit_cta2(smem_u32(mma_drain));
         mbar_wait_drain(mma_drain, 0);
@@ -196,9 +222,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int n0 = nb * Cfg::kTileN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue)) break;
+      // One lane per warp polls; the other 31 park at __syncwarp instead of
+      // hammering the barrier word in shared memory beside the tensor core.
+      bool got = true;
+      if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue));
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
       tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * Cfg::kTileN;
+#ifdef B200_GEMM_NOEPI
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (true) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
+        else mbar_arrive(&tmem_empty[acc]);
+      }
+      continue;
+#endif
 #pragma unroll 1
       for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
         uint32_t lo[32], hi[32];
@@ -232,6 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) bulk_wait_group<0>();
   }
 
+  B200_PROF_FLUSH
   tc_fence_before_sync();
   cluster_sync();  // no CTA leaves while its peer may still signal it or read its smem
   if (warp == 1) {
