@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <cstdio>
@@ -31,6 +32,7 @@
 #include "gemm_common.cuh"
 #include "kernel_cta1.cuh"
 #include "kernel_cta2.cuh"
+#include "kernel_skinny.cuh"
 #include "../../include/b200_gemm.h"
 
 // ===========================================================================
@@ -88,8 +90,8 @@ int current_device_info(DeviceInfo& out) {
 // 2-D fp16 tensor map over a row-major matrix of `rows` x `cols` (cols
 // contiguous, `ld` elements between rows), box `box_cols` x `box_rows`,
 // 128-byte swizzle, zero fill out of bounds.
-int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
-                 uint32_t box_rows, CUtensorMapL2promotion promo) {
+int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+                   uint32_t box_rows, CUtensorMapL2promotion promo) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return B200_ERR_TENSOR_MAP;
   // A zero-extent dimension is not encodable; callers never pass one.
@@ -101,6 +103,61 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
+}
+
+// Encoding a tensor map is a driver call of about a microsecond; repeated
+// GEMMs on the same buffers reuse the encoded map from a small per-thread
+// cache keyed by every field that goes into it.
+struct TmapKey {
+  const void* base;
+  uint64_t rows, cols, ld;
+  uint32_t box_cols, box_rows, promo;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box_cols == o.box_cols &&
+           box_rows == o.box_rows && promo == o.promo;
+  }
+};
+
+struct TmapCache {
+  static constexpr int kEntries = 24;
+  TmapKey key[kEntries];
+  CUtensorMap map[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+};
+
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapL2promotion promo) {
+  static thread_local TmapCache cache;
+  const TmapKey k{base, rows, cols, ld, box_cols, box_rows, static_cast<uint32_t>(promo)};
+  for (int i = 0; i < TmapCache::kEntries; ++i) {
+    if (cache.used[i] && cache.key[i] == k) {
+      *map = cache.map[i];
+      return B200_OK;
+    }
+  }
+  const int rc = encode_tmap_2d(map, base, rows, cols, ld, box_cols, box_rows, promo);
+  if (rc != B200_OK) return rc;
+  const int slot = cache.next;
+  cache.next = (cache.next + 1) % TmapCache::kEntries;
+  cache.key[slot] = k;
+  cache.map[slot] = *map;
+  cache.used[slot] = true;
+  return B200_OK;
+}
+
+// cudaFuncSetAttribute once per (kernel instantiation, device); `done` is
+// the calling launch template's own flag array (all kernels share one
+// function-pointer type, so the flags cannot live here).
+template <typename Kern>
+int ensure_smem_attr(Kern kern, int smem_bytes, std::atomic<uint8_t>* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire)) return B200_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (dev >= 0 && dev < kMaxDevices) done[dev].store(1, std::memory_order_release);
+  return B200_OK;
 }
 
 template <int BN, int STAGES, bool kBRowMajor>
@@ -119,10 +176,8 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
   if (rc) return rc;
 
   auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, kBRowMajor>;
-  // Per-function attribute; cheap, and set every call so a new device or
-  // context never sees the 48 KB default.
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess)
-    return B200_ERR_CUDA;
+  static std::atomic<uint8_t> attr_done[kMaxDevices];
+  if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<long long>(tiles, sm_count);
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m);
@@ -167,8 +222,8 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
   auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, kBRowMajor>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess)
-    return B200_ERR_CUDA;
+  static std::atomic<uint8_t> attr_done[kMaxDevices];
+  if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -181,6 +236,36 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
   kern<<<2 * grid_pairs, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+// Skinny (K <= 256) B-stationary kernel.  The grid is the largest multiple of
+// the number of 256-column N slices that fits the SMs, so every CTA keeps one
+// slice of B resident.  Returns B200_ERR_INVALID_ARGUMENT when the shape does
+// not qualify (caller falls back to another variant).
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor>
+int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc,
+                  int sm_count, cudaStream_t stream) {
+  using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
+  const int num_nb = (N + Cfg::kBN - 1) / Cfg::kBN;
+  if (K > Cfg::kMaxKBlocks * kBK || num_nb > sm_count) return B200_ERR_INVALID_ARGUMENT;
+  CUtensorMap ta, tb, tc;
+  int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  if (kBRowMajor)
+    rc = make_tmap_2d(&tb, B, K, N, ldb, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  else
+    rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, Cfg::kBN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  if (rc) return rc;
+  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor>;
+  static std::atomic<uint8_t> attr_done[kMaxDevices];
+  if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
+  const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
+  const int slots = (sm_count / num_nb) * num_nb;
+  const int grid = (int)std::min<long long>(tiles, slots);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -231,11 +316,23 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
 
   const int m = (int)M, n = (int)N, k = (int)K;
   int variant = g_variant;
+  if (variant == B200_VARIANT_AUTO && k <= 256 && (n + 255) / 256 <= dev.sm_count) {
+    // B-stationary pays for its one-off B load once a CTA has several tiles
+    // (measured: ahead from ~3 tiles per SM, behind at 1-2).
+    const long long tiles = (long long)((m + 127) / 128) * ((n + 255) / 256);
+    if (tiles >= 3LL * dev.sm_count) variant = B200_VARIANT_SKINNY;
+  }
   if (variant == B200_VARIANT_AUTO) {
     // Pairs pay off once there are enough 256 x 256 tiles to fill the GPU and
     // the K loop is long enough to amortise the pair's prologue.
     const long long pair_tiles = (long long)((m + 255) / 256) * ((n + 255) / 256);
     variant = (pair_tiles >= dev.sm_count / 2 && k >= 512) ? B200_VARIANT_PAIR : B200_VARIANT_CTA1;
+  }
+  if (variant == B200_VARIANT_SKINNY) {
+    const int rc = row_b ? launch_skinny<5, 1, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream)
+                         : launch_skinny<5, 1, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream);
+    if (rc != B200_ERR_INVALID_ARGUMENT) return rc;
+    variant = B200_VARIANT_CTA1;  // shape outside the skinny kernel's range
   }
   const int gm = group_m_override();
   if (variant == B200_VARIANT_PAIR) {
@@ -250,7 +347,7 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
 }
 
 extern "C" int b200_gemm_set_variant(int variant) {
-  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_PAIR) return B200_ERR_INVALID_ARGUMENT;
+  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_SKINNY) return B200_ERR_INVALID_ARGUMENT;
   b200::g_variant = variant;
   return B200_OK;
 }

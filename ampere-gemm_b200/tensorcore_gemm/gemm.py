@@ -123,6 +123,14 @@ def _check_operands(A: torch.Tensor, B: torch.Tensor) -> None:
         raise RuntimeError("A and B must be on the same CUDA device")
 
 
+def _current_stream(dev: int) -> int:
+    """Raw cudaStream_t of torch's current stream on `dev`."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(dev)
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
 def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tensor | None = None) -> torch.Tensor:
     """C = A @ B (B given as K x N) or A @ B.T (B given as N x K, b_col_major)."""
     M, K = A.shape
@@ -147,11 +155,15 @@ def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tens
             f"B.data_ptr%16={B.data_ptr() % 16})")
     if not _tma_ok(C, ldc):
         raise RuntimeError(f"B200 GEMM needs N to be a multiple of 8 for the fp16 output (N={N})")
-    with torch.cuda.device(A.device):
-        stream = torch.cuda.current_stream(A.device).cuda_stream
-        code = _native.gemm_f16_raw(
-            A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc,
-            _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR, stream)
+    dev = A.device.index
+    layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
+    if dev == torch.cuda.current_device():
+        code = _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
+                                    _current_stream(dev))
+    else:
+        with torch.cuda.device(dev):
+            code = _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
+                                        _current_stream(dev))
     _native.check(code, "root_gemm launch")
     return C
 

@@ -50,9 +50,10 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 side measurements")
     ap.add_argument("--case", default=None,
                     help="single-GEMM mode for profiling/tuning: MxNxK[:colb] (1 GPU, not the driver line)")
-    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "torch"],
+    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "skinny", "torch"],
                     help="kernel for --case (torch = torch.mm comparator)")
     ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"], help="inputs for --case")
+    ap.add_argument("--graph", action="store_true", help="--case: time a CUDA-graph replay (device time only)")
     return ap.parse_args()
 
 
@@ -251,6 +252,30 @@ def workload_config(n_gpus: int) -> dict:
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+def _time_graph(torch, fn, iters: int) -> float:
+    """Mean ms per call of fn(i), i = 0..iters-1, captured once in a CUDA graph
+    and replayed: device time only, no host launch gaps between calls."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(min(iters, 3)):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
 def _time_launches(torch, fn, iters: int) -> float:
     """Mean ms per call of fn() over `iters` back-to-back calls (CUDA events)."""
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -296,12 +321,13 @@ def side_measurements(torch, tg, dev, peaks) -> dict:
         for i in range(3 * nsets):
             f(i)
     iters = 40 * nsets
-    ms_row = _time_launches(torch, row, iters)
-    ms_col = _time_launches(torch, col, iters)
-    ms_mm = _time_launches(torch, mm, iters)
+    ms_row = _time_graph(torch, row, iters)
+    ms_col = _time_graph(torch, col, iters)
+    ms_mm = _time_graph(torch, mm, iters)
     gbs = lambda ms: set_bytes / (ms * 1e-3) / 1e9
     out["skinny_32768x1024x256"] = {
         "cold_l2": f"{nsets} rotating operand sets of {set_bytes / 1e6:.1f} MB (> 2x L2)",
+        "timing": "CUDA-graph replay of back-to-back launches (device time, no host gaps)",
         "algorithmic_bytes": set_bytes,
         "rowB_us": round(ms_row * 1e3, 2), "rowB_GBps": round(gbs(ms_row), 1),
         "colb_us": round(ms_col * 1e3, 2), "colb_GBps": round(gbs(ms_col), 1),
@@ -500,9 +526,10 @@ def run_case(args) -> int:
 
     for i in range(max(args.warmup, 1)):
         f(i)
-    ms = _time_launches(torch, f, args.steps)
+    ms = _time_graph(torch, f, args.steps) if args.graph else _time_launches(torch, f, args.steps)
     err = _native.last_device_error()
-    print(json.dumps({"case": args.case, "variant": args.variant, "dist": args.dist, "us": round(ms * 1e3, 2),
+    print(json.dumps({"case": args.case, "variant": args.variant, "dist": args.dist, "graph": args.graph,
+                      "us": round(ms * 1e3, 2),
                       "TFLOPs": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
                       "GBps": round(set_bytes / (ms * 1e-3) / 1e9, 1), "operand_sets": nsets,
                       "device_error_word": err}), flush=True)
