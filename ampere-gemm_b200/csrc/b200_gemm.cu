@@ -336,11 +336,11 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
   }
   const int gm = group_m_override();
   if (variant == B200_VARIANT_PAIR) {
-    const int group_m = gm ? gm : 16;  // 16 x 256-row bands: best measured on 8192^3 and 65536 x 8192^2
+    const int group_m = gm ? gm : 8;  // 8 x 256-row bands: fewest DRAM bytes measured at 8192^3
     if (row_b) return launch_tcgen05_pair<3, 2, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
     return launch_tcgen05_pair<3, 2, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
   }
-  const int group_m = gm ? gm : 16;
+  const int group_m = gm ? gm : 16;  // 16 x 128-row bands: fewest DRAM bytes measured at 8192^3
   if (row_b)
     return launch_tcgen05<256, 4, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
   return launch_tcgen05<256, 4, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);

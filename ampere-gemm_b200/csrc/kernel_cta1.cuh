@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer (one lane) ----------------
     if (lane == 0) {
+      // Measured (ncu DRAM bytes, 8192^3): A evict_normal + B evict_last reads
+      // the least; the reverse hints read 30-60 % more.
       const uint64_t pol_a = policy_evict_normal();
       const uint64_t pol_b = policy_evict_last();
       int stage = 0;
