@@ -35,6 +35,22 @@
 #include "kernel_skinny.cuh"
 #include "../../include/b200_gemm.h"
 
+namespace b200 {
+
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing ever arrives at, gives up after `limit_ns`, records
+// kDevTimeoutSelftest in the device error word and returns.
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+    mbar_wait(&bar, 0, kDevTimeoutSelftest, limit_ns);
+  }
+}
+
+}  // namespace b200
+
 // ===========================================================================
 // Host side
 // ===========================================================================
@@ -393,3 +409,13 @@ extern "C" __attribute__((visibility("default"))) int b200_gemm_debug_read_profi
   return cudaMemcpyToSymbol(b200::g_prof, zeros, sizeof(zeros)) == cudaSuccess ? 0 : -1;
 }
 #endif
+
+extern "C" int b200_gemm_selftest_bounded_wait(int64_t limit_ns) {
+  if (limit_ns <= 0 || limit_ns > 1000000000LL) return -B200_ERR_INVALID_ARGUMENT;
+  const int before = b200_gemm_last_device_error();  // clears any earlier word
+  if (before < 0) return -B200_ERR_CUDA;
+  b200::bounded_wait_selftest_kernel<<<1, 32>>>(static_cast<uint64_t>(limit_ns));
+  if (cudaGetLastError() != cudaSuccess) return -B200_ERR_CUDA;
+  const int word = b200_gemm_last_device_error();
+  return word < 0 ? -B200_ERR_CUDA : word;
+}

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevTimeoutMma = 2,        // MMA warp waited too long for a full stage / free accumulator
   kDevTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
   kDevTimeoutDrain = 4,      // abort path could not drain in-flight copies
+  kDevTimeoutSelftest = 5,   // the self-test's deliberately unsatisfied wait ran out
 };
 
 // Defined here: the library is one translation unit (csrc/b200_gemm.cu).
@@ -92,14 +93,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits until the phase of `bar` with the given parity has completed.
 // Returns false (after recording `err_code`) when the wall-clock limit passes,
 // or at once when another CTA or role has already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (device_error_raised()) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         raise_device_error(err_code);
         return false;
       }

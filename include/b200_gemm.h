@@ -84,6 +84,15 @@ B200_API int b200_gemm_sm_count(void);
  * the B layout). */
 B200_API int b200_gemm_set_variant(int variant);
 
+/* Self-test of the kernels' failure path: launches one thread that waits on
+ * a barrier nothing arrives at, with a bounded wait of `limit_ns`
+ * (1 ns .. 1 s), on the legacy default stream of the current device.  The
+ * wait gives up, records cause 5 in the device error word and the kernel
+ * returns; the context stays usable.  Returns the error word it read (5 when
+ * the bounded wait works; the word is cleared again), or a negative
+ * B200_ERR_* code.  No counterpart in the reference. */
+B200_API int b200_gemm_selftest_bounded_wait(int64_t limit_ns);
+
 /* Library ABI version (major * 100 + minor). */
 B200_API int b200_gemm_version(void);
 

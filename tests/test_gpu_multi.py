@@ -1,0 +1,70 @@
+"""GPU, 2+ devices: row-sharded GEMM on each rank plus the NCCL all-gather of C.
+
+Skipped when fewer than two GPUs are visible.  Each rank is its own process
+(one process per GPU); no kernel waits on another GPU.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for p in (str(repo), str(repo / "ampere-gemm_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensorcore_gemm import _native, sharded
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        M, N, K = 1000, 264, 512          # ragged: the last shard is short
+        A, B = oracle.make_inputs(M, N, K, dist="normal", seed_a=31, seed_b=32, std=0.02)
+        lo, hi = sharded.row_shard_bounds(M, world, rank)
+        Cs = sharded.sharded_gemm(A[lo:hi].to(dev), B.to(dev))
+        full = sharded.all_gather_rows(Cs, M)
+        torch.cuda.synchronize()
+        ref = A.float() @ B.float()
+        err = (full.float().cpu() - ref).abs().max().item()
+        bound = 2e-3 * K ** 0.5 * ref.pow(2).mean().sqrt().item()
+        q.put((rank, err <= bound and _native.last_device_error() == 0, err, bound))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_sharded_gemm_and_all_gather(native_lib):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    res = [q.get(timeout=30) for _ in procs]
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(ok for _, ok, _, _ in res), res
