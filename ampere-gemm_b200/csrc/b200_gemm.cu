@@ -306,30 +306,40 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // ===========================================================================
 // C ABI
 // ===========================================================================
-extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                             int64_t ldb, int64_t ldc, int b_layout, void* stream_ptr) {
-  using namespace b200;
+namespace b200 {
+namespace {
+
+// Arguments common to every entry point.  Returns B200_OK, or an error code;
+// sets *nothing_to_do when the output is empty.
+int validate_args(const void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                  int b_layout, const void* A, const void* B, bool* nothing_to_do) {
+  *nothing_to_do = false;
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   if (b_layout != B200_B_ROW_MAJOR && b_layout != B200_B_COL_MAJOR) return B200_ERR_INVALID_ARGUMENT;
   const int64_t kMax = 0x7fffffff;
   if (M > kMax || N > kMax || K > kMax) return B200_ERR_TOO_LARGE;
-  if (M == 0 || N == 0) return B200_OK;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  if (!C) return B200_ERR_INVALID_ARGUMENT;
-  if (ldc < N) return B200_ERR_INVALID_ARGUMENT;
-  if (!aligned16(C) || (ldc % 8) != 0) return B200_ERR_MISALIGNED;
-  DeviceInfo dev;
-  if (int rc = current_device_info(dev)) return rc;
-  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  if (M == 0 || N == 0) {
+    *nothing_to_do = true;
+    return B200_OK;
+  }
+  if (!C || ldc < N) return B200_ERR_INVALID_ARGUMENT;
+  if (K > 0) {
+    const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+    if (!A || !B || lda < K || ldb < (row_b ? N : K)) return B200_ERR_INVALID_ARGUMENT;
+  }
+  return B200_OK;
+}
+
+bool pitch_ok(const void* p, int64_t ld) { return aligned16(p) && (ld % 8) == 0; }
+
+// C = A * B on operands that already satisfy TMA's alignment rules.
+int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                 int64_t ldc, int b_layout, const DeviceInfo& dev, cudaStream_t stream) {
   if (K == 0) {
     // Empty reduction: C is all zeros.
     return cudaMemset2DAsync(C, ldc * 2, 0, N * 2, M, stream) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
-  if (!A || !B) return B200_ERR_INVALID_ARGUMENT;
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
-  if (lda < K || ldb < (row_b ? N : K)) return B200_ERR_INVALID_ARGUMENT;
-  if (!aligned16(A) || !aligned16(B) || (lda % 8) != 0 || (ldb % 8) != 0) return B200_ERR_MISALIGNED;
-
   const int m = (int)M, n = (int)N, k = (int)K;
   int variant = g_variant;
   if (variant == B200_VARIANT_AUTO && k <= 256 && (n + 255) / 256 <= dev.sm_count) {
@@ -362,6 +372,141 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
   return launch_tcgen05<256, 4, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
 }
 
+// Copies a rows x cols fp16 matrix between row pitches (elements).
+__global__ void pitched_copy_f16_kernel(const uint16_t* __restrict__ src, int64_t src_ld, uint16_t* __restrict__ dst,
+                                        int64_t dst_ld, int64_t rows, int64_t cols) {
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += (int64_t)gridDim.x * blockDim.x)
+      dst[r * dst_ld + c] = src[r * src_ld + c];
+}
+
+int pitched_copy(const void* src, int64_t src_ld, void* dst, int64_t dst_ld, int64_t rows, int64_t cols,
+                 cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return B200_OK;
+  const unsigned gx = (unsigned)std::min<int64_t>((cols + 255) / 256, 64);
+  const unsigned gy = (unsigned)std::min<int64_t>(rows, 65535);
+  pitched_copy_f16_kernel<<<dim3(gx, gy), 256, 0, stream>>>(static_cast<const uint16_t*>(src), src_ld,
+                                                             static_cast<uint16_t*>(dst), dst_ld, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+// Workspace plan for operands whose base or row pitch TMA cannot describe:
+// each such operand gets a copy with a 16-byte row pitch (pitch rounded up
+// to 8 elements) at a 256-byte aligned offset.  Unaligned C is computed into
+// its copy and copied back.
+struct RepackPlan {
+  bool a = false, b = false, c = false;
+  int64_t lda2 = 0, ldb2 = 0, ldc2 = 0;
+  int64_t off_a = 0, off_b = 0, off_c = 0, bytes = 0;
+};
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+RepackPlan plan_repack(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb, int64_t ldc, int b_layout) {
+  RepackPlan p;
+  const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+  if (K > 0) {
+    p.a = !pitch_ok(A, lda);
+    p.b = !pitch_ok(B, ldb);
+  }
+  p.c = !pitch_ok(C, ldc);
+  int64_t off = 0;
+  if (p.a) {
+    p.lda2 = round_up(K, 8);
+    p.off_a = off;
+    off = round_up(off + M * p.lda2 * 2, 256);
+  }
+  if (p.b) {
+    const int64_t rows = row_b ? K : N, cols = row_b ? N : K;
+    p.ldb2 = round_up(cols, 8);
+    p.off_b = off;
+    off = round_up(off + rows * p.ldb2 * 2, 256);
+  }
+  if (p.c) {
+    p.ldc2 = round_up(N, 8);
+    p.off_c = off;
+    off = round_up(off + M * p.ldc2 * 2, 256);
+  }
+  p.bytes = off;
+  return p;
+}
+
+// Repack (as planned), multiply, copy C back; `ws` is device memory of at
+// least plan.bytes, 256-byte aligned.
+int gemm_repacked(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                  int64_t ldc, int b_layout, const RepackPlan& p, uint8_t* ws, const DeviceInfo& dev,
+                  cudaStream_t stream) {
+  const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+  const void* a = A;
+  const void* b = B;
+  void* c = C;
+  int64_t la = lda, lb = ldb, lc = ldc;
+  int rc = B200_OK;
+  if (p.a) {
+    a = ws + p.off_a;
+    la = p.lda2;
+    if ((rc = pitched_copy(A, lda, ws + p.off_a, la, M, K, stream))) return rc;
+  }
+  if (p.b) {
+    b = ws + p.off_b;
+    lb = p.ldb2;
+    if ((rc = pitched_copy(B, ldb, ws + p.off_b, lb, row_b ? K : N, row_b ? N : K, stream))) return rc;
+  }
+  if (p.c) {
+    c = ws + p.off_c;
+    lc = p.ldc2;
+  }
+  if ((rc = gemm_aligned(a, b, c, M, N, K, la, lb, lc, b_layout, dev, stream))) return rc;
+  if (p.c) rc = pitched_copy(c, lc, C, ldc, M, N, stream);
+  return rc;
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                             int64_t ldb, int64_t ldc, int b_layout, void* stream_ptr) {
+  using namespace b200;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return rc;
+  if (done) return B200_OK;
+  if (!pitch_ok(C, ldc)) return B200_ERR_MISALIGNED;
+  if (K > 0 && (!pitch_ok(A, lda) || !pitch_ok(B, ldb))) return B200_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, static_cast<cudaStream_t>(stream_ptr));
+}
+
+extern "C" int64_t b200_gemm_workspace_size(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                                            int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout) {
+  using namespace b200;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return -rc;
+  if (done) return 0;
+  return plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout).bytes;
+}
+
+extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                int64_t ldb, int64_t ldc, int b_layout, void* workspace, int64_t workspace_bytes,
+                                void* stream_ptr) {
+  using namespace b200;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return rc;
+  if (done) return B200_OK;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
+  if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, stream);
+  if (!workspace || workspace_bytes < p.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return B200_ERR_WORKSPACE;
+  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, b_layout, p, static_cast<uint8_t*>(workspace), dev,
+                       stream);
+}
+
 extern "C" int b200_gemm_set_variant(int variant) {
   if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_SKINNY) return B200_ERR_INVALID_ARGUMENT;
   b200::g_variant = variant;
@@ -378,6 +523,7 @@ extern "C" const char* b200_gemm_strerror(int code) {
     case B200_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled unavailable or rejected the tensor map";
     case B200_ERR_DEVICE: return "device error word set: a bounded wait inside the kernel timed out";
     case B200_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case B200_ERR_WORKSPACE: return "workspace missing, too small, or not 256-byte aligned (see b200_gemm_workspace_size)";
     default: return "unknown error code";
   }
 }

@@ -19,8 +19,10 @@ Differences from the reference, all deliberate:
   * No silent fallback.  The reference returned ``torch.matmul(A, B)`` for any
     input it could not run (gemm.py:219-221), on CPU too.  Here unsupported
     inputs raise ``RuntimeError``; nothing computes on the CPU.
-  * Any M, N, K is accepted (TMA zero fill / clipped stores), not only
-    M % 256 == N % 128 == K % 32 == 0 with K >= 64 (gemm.py:185-192).
+  * Any M, N, K is accepted (TMA zero fill / clipped stores; operands whose
+    row pitch is not 16-byte aligned are re-pitched through a workspace on
+    the GPU), not only M % 256 == N % 128 == K % 32 == 0 with K >= 64
+    (gemm.py:185-192).
   * ``gemm`` in a colb mode does not transpose B first (gemm.py:227-228): the
     kernel reads row-major B with an MN-major shared-memory descriptor, which
     gives the same product without the extra HBM pass.
@@ -82,11 +84,12 @@ def _tma_ok(t: torch.Tensor, ld: int) -> bool:
 
 
 def is_supported(A: torch.Tensor, B: torch.Tensor) -> bool:
-    """True when ``gemm(A, B)`` runs on the B200 kernel.
+    """True when ``gemm(A, B)`` runs on the B200 kernels.
 
-    Reference predicate: gemm.py:173-192.  Here the tile-multiple conditions
-    are gone; what remains is CUDA, fp16, 2-D, matching inner dimension, and
-    16-byte row pitches for TMA (K and N multiples of 8 once contiguous).
+    Reference predicate: gemm.py:173-192.  The tile-multiple and contiguity
+    conditions are gone (TMA zero fill, clipped stores, strided views, and a
+    re-pitching workspace for odd K/N); what remains is CUDA, fp16, 2-D, one
+    device and a matching inner dimension.
     """
     if not (isinstance(A, torch.Tensor) and isinstance(B, torch.Tensor)):
         return False
@@ -98,11 +101,7 @@ def is_supported(A: torch.Tensor, B: torch.Tensor) -> bool:
         return False
     if A.dtype != torch.float16 or B.dtype != torch.float16:
         return False
-    if A.device != B.device:
-        return False
-    k = A.shape[1]
-    n = B.shape[1]
-    return k % _ALIGN_ELEMS == 0 and n % _ALIGN_ELEMS == 0
+    return A.device == B.device
 
 
 def _check_operands(A: torch.Tensor, B: torch.Tensor) -> None:
@@ -131,6 +130,18 @@ def _current_stream(dev: int) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev) -> int:
+    stream = _current_stream(dev)
+    if (K == 0 or (_tma_ok(A, lda) and _tma_ok(B, ldb))) and _tma_ok(C, ldc):
+        return _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout, stream)
+    # An operand TMA cannot address (odd K or N, or storage not 16-byte
+    # aligned): the library re-pitches it through a workspace on the GPU.
+    ws_bytes = _native.workspace_size(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
+    return _native.gemm_f16_ws_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
+                                   ws.data_ptr(), ws_bytes, stream)
+
+
 def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tensor | None = None) -> torch.Tensor:
     """C = A @ B (B given as K x N) or A @ B.T (B given as N x K, b_col_major)."""
     M, K = A.shape
@@ -148,22 +159,13 @@ def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tens
     if M == 0 or N == 0:
         return C
     ldc = C.stride(0) if N > 1 else max(1, N)
-    if K > 0 and not (_tma_ok(A, lda) and _tma_ok(B, ldb)):
-        raise RuntimeError(
-            "B200 GEMM needs 16-byte aligned operands with row pitches that are multiples of 8 "
-            f"elements (got lda={lda}, ldb={ldb}, A.data_ptr%16={A.data_ptr() % 16}, "
-            f"B.data_ptr%16={B.data_ptr() % 16})")
-    if not _tma_ok(C, ldc):
-        raise RuntimeError(f"B200 GEMM needs N to be a multiple of 8 for the fp16 output (N={N})")
     dev = A.device.index
     layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
-    if dev == torch.cuda.current_device():
-        code = _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
-                                    _current_stream(dev))
-    else:
+    if dev != torch.cuda.current_device():
         with torch.cuda.device(dev):
-            code = _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
-                                        _current_stream(dev))
+            code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev)
+    else:
+        code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev)
     _native.check(code, "root_gemm launch")
     return C
 
@@ -216,9 +218,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, mode: str = "wmma", out: torch.Tensor
         _check_operands(A, B)
         if A.shape[1] != B.shape[0]:
             raise RuntimeError("Inner dimensions must match")
-        raise RuntimeError(
-            f"unsupported operands for the B200 GEMM: K={A.shape[1]} and N={B.shape[1]} "
-            "must be multiples of 8 (16-byte TMA row pitch)")
+        raise RuntimeError("unsupported operands for the B200 GEMM")
     if out is not None:
         if (out.dtype != torch.float16 or out.device != A.device or tuple(out.shape) != (A.shape[0], B.shape[1])
                 or (out.shape[1] > 1 and out.stride(1) != 1)):

@@ -46,6 +46,7 @@ extern "C" {
 #define B200_ERR_TENSOR_MAP 5       /* cuTensorMapEncodeTiled unavailable or rejected the map */
 #define B200_ERR_DEVICE 6           /* the device error word was set (a bounded wait timed out) */
 #define B200_ERR_UNSUPPORTED_DEVICE 7 /* current device is not sm_100 */
+#define B200_ERR_WORKSPACE 8        /* workspace missing, too small or not 256-byte aligned */
 
 /*
  * C = A * B on `stream` (a cudaStream_t; NULL = legacy default stream).
@@ -57,6 +58,28 @@ extern "C" {
  */
 B200_API int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                   int64_t ldb, int64_t ldc, int b_layout, void* stream);
+
+/*
+ * Operands that TMA cannot address directly (a base pointer not 16-byte
+ * aligned, or a leading dimension that is not a multiple of 8 elements --
+ * e.g. K or N odd) are handled by this pair of calls.  The reference accepted
+ * such shapes only through its torch.matmul fallback (tensorcore_gemm/gemm.py
+ * :185-192, 219-221) and ran them out of bounds through gemm_pretransposed
+ * (gemm.py:209-216).
+ *
+ * b200_gemm_workspace_size returns the device workspace in bytes that
+ * b200_gemm_f16_ws needs for these operands (0 when every operand is already
+ * TMA-compatible), or a negative B200_ERR_* code.  b200_gemm_f16_ws copies each
+ * incompatible operand into the workspace with a 16-byte row pitch, multiplies,
+ * and copies C back when C itself was incompatible; all on `stream`.  The
+ * workspace must be 256-byte aligned device memory of at least that size and
+ * must not be reused until the call's work on `stream` has finished.
+ */
+B200_API int64_t b200_gemm_workspace_size(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                                          int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout);
+B200_API int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                              int64_t ldb, int64_t ldc, int b_layout, void* workspace, int64_t workspace_bytes,
+                              void* stream);
 
 /* Human-readable text of a return code (static storage). Counterpart of the
  * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */

@@ -81,3 +81,19 @@ def test_set_variant_validation(native_lib):
     assert native_lib.b200_gemm_set_variant(-1) == _native.B200_ERR_INVALID_ARGUMENT
     for v in ("pair", "cta1", "auto"):
         _native.set_variant(v)
+
+
+def test_workspace_size_plan(native_lib):
+    """Host-side workspace arithmetic: 16-byte pitches, 256-byte aligned parts."""
+    from tensorcore_gemm import _native
+
+    A, B, C = 0x10000, 0x20000, 0x30000          # aligned fake addresses (never dereferenced)
+    ws = lambda *a: native_lib.b200_gemm_workspace_size(*a)
+    assert ws(A, B, C, 64, 64, 64, 64, 64, 64, 0) == 0                 # nothing to re-pitch
+    assert ws(A, B, C, 10, 16, 7, 7, 16, 16, 0) == 256                  # A: 10 x 8 x 2 = 160 -> 256
+    assert ws(A, B, C, 10, 17, 16, 16, 17, 17, 0) == 768 + 512          # B 16x24x2=768; C 10x24x2=480 -> 512
+    # B col-major N x K with odd K: both A and B re-pitched
+    assert ws(A, B, C, 4, 8, 9, 9, 9, 8, 1) == 256 + 256
+    assert ws(A + 2, B, C, 4, 8, 8, 8, 8, 8, 0) == 256                  # misaligned base only
+    assert ws(A, B, C, 0, 8, 8, 8, 8, 8, 0) == 0                        # empty output
+    assert ws(A, B, C, 4, 8, 8, 4, 8, 8, 0) == -_native.B200_ERR_INVALID_ARGUMENT   # lda < K

@@ -161,12 +161,61 @@ def test_strided_views_without_copies(cuda_device, variant):
     assert_parity(C, A.float() @ B.float(), 256)
 
 
-def test_unsupported_alignment_raises(cuda_device, native_lib):
-    A = torch.ones((16, 12), dtype=torch.float16, device=cuda_device)
-    B = torch.ones((12, 16), dtype=torch.float16, device=cuda_device)
-    assert not tg.is_supported(A, B)
-    with pytest.raises(RuntimeError):
-        tg.gemm(A, B)
+ODD = [(1, 1, 1), (3, 5, 7), (37, 23, 41), (130, 257, 100), (257, 300, 513), (64, 9, 1000), (2049, 129, 255)]
+
+
+@pytest.mark.parametrize("M,N,K", ODD)
+@pytest.mark.parametrize("colb", [False, True])
+def test_odd_pitches_through_workspace(cuda_device, variant, M, N, K, colb):
+    """K or N not a multiple of 8: operands are re-pitched on the GPU."""
+    A, B = _inputs(M, N, K, cuda_device, seed=M * 3 + N + K)
+    assert tg.is_supported(A, B)
+    if colb:
+        C = tg.gemm_pretransposed(A, B.t().contiguous(), mode="reg_pingpong_256_colb")
+    else:
+        C = tg.gemm(A, B)
+    torch.cuda.synchronize()
+    assert C.shape == (M, N) and C.is_contiguous()
+    oracle_check(C, A, B)
+    _no_device_error()
+
+
+def test_misaligned_storage_and_strided_output(cuda_device, variant):
+    """Bases off the 16-byte grid and an output view with an odd row pitch."""
+    M, N, K = 300, 200, 264
+    A0, B0 = _inputs(M, N, K, cuda_device, seed=77)
+    abuf = torch.empty(M * K + 1, dtype=torch.float16, device=cuda_device)
+    A = abuf[1:].view(M, K)
+    A.copy_(A0)
+    bbuf = torch.empty(K * N + 3, dtype=torch.float16, device=cuda_device)
+    B = bbuf[3:].view(K, N)
+    B.copy_(B0)
+    cbuf = torch.full((M, N + 5), 9.0, dtype=torch.float16, device=cuda_device)
+    C = cbuf[:, 1:1 + N]
+    tg.gemm(A, B, out=C)
+    torch.cuda.synchronize()
+    assert_parity(C, fp32_ref(A0, B0), K)
+    assert (cbuf[:, 0] == 9.0).all() and (cbuf[:, 1 + N:] == 9.0).all()
+    _no_device_error()
+
+
+def test_workspace_abi(cuda_device, native_lib):
+    """b200_gemm_f16 refuses odd pitches; the _ws entry takes them with enough workspace."""
+    M, N, K = 40, 24, 36
+    A, B = _inputs(M, N, K, cuda_device, seed=5)
+    Abig = torch.zeros((M, 37), dtype=torch.float16, device=cuda_device)
+    Abig[:, :K] = A
+    C = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    args = (Abig.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, 37, N, N, _native.B200_B_ROW_MAJOR)
+    assert _native.gemm_f16_raw(*args, s) == _native.B200_ERR_MISALIGNED
+    need = _native.workspace_size(*args)
+    assert need >= M * 40 * 2
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    assert _native.gemm_f16_ws_raw(*args, ws.data_ptr(), need - 256, s) == _native.B200_ERR_WORKSPACE
+    assert _native.gemm_f16_ws_raw(*args, ws.data_ptr(), need, s) == 0
+    torch.cuda.synchronize()
+    assert_parity(C, fp32_ref(A, B), K)
 
 
 def test_current_stream_is_used(cuda_device, native_lib):
