@@ -524,6 +524,7 @@ extern "C" const char* b200_gemm_strerror(int code) {
     case B200_ERR_DEVICE: return "device error word set: a bounded wait inside the kernel timed out";
     case B200_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case B200_ERR_WORKSPACE: return "workspace missing, too small, or not 256-byte aligned (see b200_gemm_workspace_size)";
+    case B200_ERR_SCRATCH_LIMIT: return "operands need more re-pitch scratch than the 32 MiB built into b200_gemm_f16_noalloc";
     default: return "unknown error code";
   }
 }
@@ -564,4 +565,64 @@ extern "C" int b200_gemm_selftest_bounded_wait(int64_t limit_ns) {
   if (cudaGetLastError() != cudaSuccess) return -B200_ERR_CUDA;
   const int word = b200_gemm_last_device_error();
   return word < 0 ? -B200_ERR_CUDA : word;
+}
+
+// ===========================================================================
+// Allocation-free entry point (b200_gemm_f16_noalloc)
+//
+// Same product as b200_gemm_f16_ws, for callers that may not allocate device
+// memory at all: the re-pitch copies live in one fixed scratch array compiled
+// into this library.  Every GPU that loads the library holds the array
+// (kNoAllocScratchBytes) until the process exits.
+// ===========================================================================
+namespace b200 {
+
+constexpr int64_t kNoAllocScratchBytes = 32ll << 20;  // 32 MiB
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[kMaxDevices] = {};
+
+// The array's name is only a host-side handle; the device address comes from
+// cudaGetSymbolAddress, asked once per device with that device current.
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return B200_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200_OK;
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                     int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream_ptr) {
+  using namespace b200;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return rc;
+  if (done) return B200_OK;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
+  if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, stream);
+  if (p.bytes > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
+  uint8_t* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // Nothing in the scratch has to start at zero: the call writes every byte it
+  // later reads (the re-pitched operand rows, and all of C's copy) first.
+  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, b_layout, p, scratch, dev, stream);
 }

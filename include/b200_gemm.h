@@ -47,6 +47,7 @@ extern "C" {
 #define B200_ERR_DEVICE 6           /* the device error word was set (a bounded wait timed out) */
 #define B200_ERR_UNSUPPORTED_DEVICE 7 /* current device is not sm_100 */
 #define B200_ERR_WORKSPACE 8        /* workspace missing, too small or not 256-byte aligned */
+#define B200_ERR_SCRATCH_LIMIT 9    /* b200_gemm_f16_noalloc: more scratch needed than it has */
 
 /*
  * C = A * B on `stream` (a cudaStream_t; NULL = legacy default stream).
@@ -80,6 +81,27 @@ B200_API int64_t b200_gemm_workspace_size(const void* A, const void* B, const vo
 B200_API int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                               int64_t ldb, int64_t ldc, int b_layout, void* workspace, int64_t workspace_bytes,
                               void* stream);
+
+/*
+ * Allocation-free variant of b200_gemm_f16_ws.  No counterpart in the
+ * reference.  For callers that must not allocate device memory: code whose
+ * device memory belongs to a host framework's pool or arena that forbids side
+ * allocations, and latency-critical paths that cannot take cudaMalloc's
+ * implicit device synchronisation.  Operands that need re-pitching are copied
+ * into a fixed 32 MiB scratch array compiled into this library (every GPU that
+ * loads the library keeps it until the process exits); the call itself
+ * allocates nothing.  Returns B200_ERR_SCRATCH_LIMIT when the re-pitched
+ * operands (b200_gemm_workspace_size) would exceed 32 MiB; operands that need
+ * no re-pitch are not limited.
+ *
+ * The first call on a device looks up the scratch array's device address
+ * (once per device); make that first call before any stream capture.  All
+ * calls share the one array and it keeps the last call's contents, so calls
+ * whose work overlaps on the GPU (other streams, other host threads) race on
+ * it: order them on one stream or synchronise between them.
+ */
+B200_API int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                   int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream);
 
 /* Human-readable text of a return code (static storage). Counterpart of the
  * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */
