@@ -365,6 +365,7 @@ def run_b200(args) -> int:
 
     import tensorcore_gemm as tg
     from tensorcore_gemm import _native, sharded
+    from tensorcore_gemm.streamed import gemm_streamed
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -432,10 +433,9 @@ def run_b200(args) -> int:
     C_h = torch.empty((m, N_DIM), dtype=torch.float16).pin_memory()
 
     def e2e_step():
-        A.copy_(A_h, non_blocking=True)
-        B.copy_(B_h, non_blocking=True)
-        tg.gemm(A, B, out=C)
-        C_h.copy_(C, non_blocking=True)
+        # Public host-operand API: A and B copied in, C copied out, in
+        # row chunks pipelined over three streams.
+        gemm_streamed(A_h, B_h, out=C_h)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -472,7 +472,8 @@ def run_b200(args) -> int:
             "pct_nominal_dense_fp16_peak": round(100 * value / world / 2250.0, 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(2 * (m * K_DIM + K_DIM * N_DIM)),
-                    "d2h_bytes_per_step": int(2 * m * N_DIM), "steps": e2e_steps},
+                    "d2h_bytes_per_step": int(2 * m * N_DIM), "steps": e2e_steps,
+                    "api": "tensorcore_gemm.streamed.gemm_streamed (pinned host A, B, C; row chunks over 3 streams)"},
             "gpu_launches": args.steps,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
             "device_error_word": dev_err,

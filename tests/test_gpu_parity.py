@@ -239,3 +239,20 @@ def test_variants_deterministic_and_within_bound(cuda_device, native_lib):
             _native.set_variant("auto")
         assert torch.equal(C1, C2)
         assert_parity(C1, ref, 2048, v)
+
+
+@pytest.mark.parametrize("M,N,K,chunk", [(1000, 264, 320, 256), (4096, 512, 1024, None), (300, 24, 40, 64)])
+def test_streamed_host_operands(cuda_device, native_lib, M, N, K, chunk):
+    from tensorcore_gemm.streamed import gemm_streamed
+
+    A, B = oracle.make_inputs(M, N, K, seed_a=91, seed_b=92)
+    Ah, Bh = A.pin_memory(), B.pin_memory()
+    C = gemm_streamed(Ah, Bh, chunk_rows=chunk)
+    torch.cuda.synchronize()
+    assert not C.is_cuda and C.shape == (M, N)
+    assert_parity(C, A.float() @ B.float(), K)
+    # B already on the device, result into a CUDA tensor
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    gemm_streamed(Ah, Bh.to(cuda_device), out=out, chunk_rows=chunk)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), C)
