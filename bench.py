@@ -81,15 +81,20 @@ def cpu_model() -> str:
 # ---------------------------------------------------------------------------
 # nvidia-smi clock sampling during the timed region
 # ---------------------------------------------------------------------------
-CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+CLOCK_FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
 
 class ClockSampler:
+    """nvidia-smi samples every 20 ms; `summary` keeps those taken inside the
+    window marked with `mark_start` / `mark_end` (or, for a window shorter than
+    the sampling interval, the samples nearest to it)."""
+
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -99,8 +104,15 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
-        time.sleep(0.05)
+        time.sleep(0.3)  # let nvidia-smi start sampling before the timed region
         return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+        time.sleep(0.05)
 
     def __exit__(self, *exc):
         self.lines = []
@@ -115,25 +127,31 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
-        sm, smax, reasons = [], None, set()
+        import datetime
+
+        rows = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in getattr(self, "lines", []):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, smax = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+            active = {n for n, v in zip(names, parts[6:10]) if v.lower().startswith("active")}
+            rows.append((ts, sm, smax, active))
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+            if not inside:  # window shorter than the sampling interval
+                inside = sorted(rows, key=lambda r: abs(r[0] - 0.5 * (self.t0 + self.t1)))[:2]
+            rows = inside
+        reasons = set().union(*(r[3] for r in rows))
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": rows[-1][2],
+                "reasons": sorted(reasons), "samples": len(rows)}
 
 
 # ---------------------------------------------------------------------------
@@ -407,14 +425,16 @@ def run_b200(args) -> int:
 
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local_rank) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        clocks.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
         ev1.synchronize()
+        clocks.mark_end()
     torch.cuda.synchronize()
     barrier()
     ms_local = ev0.elapsed_time(ev1)
@@ -475,7 +495,8 @@ def run_b200(args) -> int:
                     "d2h_bytes_per_step": int(2 * m * N_DIM), "steps": e2e_steps,
                     "api": "tensorcore_gemm.streamed.gemm_streamed (pinned host A, B, C; row chunks over 3 streams)"},
             "gpu_launches": args.steps,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
             "device_error_word": dev_err,
         }
         if cpu is not None:
