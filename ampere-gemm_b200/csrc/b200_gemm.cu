@@ -223,10 +223,10 @@ int max_active_pairs(Kern kern, int smem_bytes, int sm_count) {
   return n;
 }
 
-template <int STAGES, int KSUB, bool kBRowMajor>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor>
 int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
                         int64_t ldc, int sm_count, int group_m, cudaStream_t stream) {
-  using Cfg = PairConfig<STAGES, KSUB>;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB>;
   CUtensorMap ta, tb, tc;
   int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
@@ -237,7 +237,7 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, kBRowMajor>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
@@ -285,6 +285,39 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
+// Kernel choice for K > 256.  Each persistent variant runs its tiles in waves
+// of `slots` concurrent tiles; the last wave is usually partial, so the
+// estimate is  waves * (per-SM tile work) / (relative per-SM rate).  Rates are
+// measured steady-state throughputs relative to the wide pair (8192^3:
+// 1.00 wide pair, 0.96 pair, 0.93 one-CTA); the model reproduces the best
+// measured variant on 2048^3 .. 8192^3, 4096 x 8192 x 4096, 8192 x 4096 x 4096,
+// 4000 x 6000 x 3000 and 65536 x 8192 x 8192.
+int pick_tensor_variant(int m, int n, int k, int sm_count) {
+  if (k < 512) return B200_VARIANT_CTA1;  // a pair's prologue is not amortised
+  struct Opt {
+    int variant, tile_m, tile_n, slots;
+    double per_sm_work, rate;
+  };
+  const int pairs = sm_count / 2;
+  const Opt opts[3] = {
+      {B200_VARIANT_PAIR_WIDE, 512, 256, pairs, 256.0 * 256.0, 1.00},
+      {B200_VARIANT_PAIR, 256, 256, pairs, 128.0 * 256.0, 0.96},
+      {B200_VARIANT_CTA1, 128, 256, sm_count, 128.0 * 256.0, 0.93},
+  };
+  int best = B200_VARIANT_CTA1;
+  double best_cost = 1e300;
+  for (const Opt& o : opts) {
+    const long long tiles = (long long)((m + o.tile_m - 1) / o.tile_m) * ((n + o.tile_n - 1) / o.tile_n);
+    const long long waves = (tiles + o.slots - 1) / o.slots;
+    const double cost = (double)waves * o.per_sm_work / o.rate;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = o.variant;
+    }
+  }
+  return best;
+}
+
 // Process-wide kernel-variant override (b200_gemm_set_variant).
 int g_variant = B200_VARIANT_AUTO;
 
@@ -292,8 +325,7 @@ int g_variant = B200_VARIANT_AUTO;
 int group_m_override() {
   static int v = [] {
     const char* e = std::getenv("B200_GEMM_GROUP_M");
-    int x = e ? std::atoi(e) : 0;
-    return x > 0 ? x : 0;
+    return e ? std::atoi(e) : 0;  // negative: bands of column blocks
   }();
   return v;
 }
@@ -348,12 +380,7 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
     const long long tiles = (long long)((m + 127) / 128) * ((n + 255) / 256);
     if (tiles >= 3LL * dev.sm_count) variant = B200_VARIANT_SKINNY;
   }
-  if (variant == B200_VARIANT_AUTO) {
-    // Pairs pay off once there are enough 256 x 256 tiles to fill the GPU and
-    // the K loop is long enough to amortise the pair's prologue.
-    const long long pair_tiles = (long long)((m + 255) / 256) * ((n + 255) / 256);
-    variant = (pair_tiles >= dev.sm_count / 2 && k >= 512) ? B200_VARIANT_PAIR : B200_VARIANT_CTA1;
-  }
+  if (variant == B200_VARIANT_AUTO) variant = pick_tensor_variant(m, n, k, dev.sm_count);
   if (variant == B200_VARIANT_SKINNY) {
     const int rc = row_b ? launch_skinny<5, 1, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream)
                          : launch_skinny<5, 1, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream);
@@ -361,10 +388,18 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
     variant = B200_VARIANT_CTA1;  // shape outside the skinny kernel's range
   }
   const int gm = group_m_override();
+  if (variant == B200_VARIANT_PAIR_WIDE) {
+    // Raster (measured DRAM bytes): when A is much taller than B is wide,
+    // bands of 16 column blocks; otherwise bands of 8 row blocks.
+    const int group_m = gm ? gm : (m >= 4LL * n ? -16 : 8);
+    if (row_b)
+      return launch_tcgen05_pair<4, 1, 2, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    return launch_tcgen05_pair<4, 1, 2, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+  }
   if (variant == B200_VARIANT_PAIR) {
     const int group_m = gm ? gm : 8;  // 8 x 256-row bands: fewest DRAM bytes measured at 8192^3
-    if (row_b) return launch_tcgen05_pair<3, 2, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
-    return launch_tcgen05_pair<3, 2, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    if (row_b) return launch_tcgen05_pair<3, 2, 1, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    return launch_tcgen05_pair<3, 2, 1, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
   }
   const int group_m = gm ? gm : 16;  // 16 x 128-row bands: fewest DRAM bytes measured at 8192^3
   if (row_b)
@@ -508,7 +543,7 @@ extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M
 }
 
 extern "C" int b200_gemm_set_variant(int variant) {
-  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_SKINNY) return B200_ERR_INVALID_ARGUMENT;
+  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_PAIR_WIDE) return B200_ERR_INVALID_ARGUMENT;
   b200::g_variant = variant;
   return B200_OK;
 }

@@ -59,19 +59,32 @@ struct TileConfig {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-// Persistent tile order: bands of `group_m` row-blocks; inside a band the row
-// block changes fastest, so CTAs that run together share B panels and a small
-// set of A panels in L2.
+// Persistent tile order.  group_m > 0: bands of group_m row blocks, row block
+// fastest inside a band (a band of A stays hot while B streams).  group_m < 0:
+// bands of -group_m column blocks, column block fastest (a band of B stays hot
+// and each A panel is finished by consecutive tiles, then dropped) -- the
+// better order when A is much larger than B.
 struct TileScheduler {
   int num_m, num_n, group_m;
   __device__ __forceinline__ void tile_coords(int t, int& mb, int& nb) const {
-    const int per_band = group_m * num_n;
-    const int band = t / per_band;
-    const int first_m = band * group_m;
-    const int gsize = min(group_m, num_m - first_m);
-    const int r = t - band * per_band;
-    mb = first_m + r % gsize;
-    nb = r / gsize;
+    if (group_m > 0) {
+      const int per_band = group_m * num_n;
+      const int band = t / per_band;
+      const int first_m = band * group_m;
+      const int gsize = min(group_m, num_m - first_m);
+      const int r = t - band * per_band;
+      mb = first_m + r % gsize;
+      nb = r / gsize;
+    } else {
+      const int gn = -group_m;
+      const int per_band = gn * num_m;
+      const int band = t / per_band;
+      const int first_n = band * gn;
+      const int gsize = min(gn, num_n - first_n);
+      const int r = t - band * per_band;
+      nb = first_n + r % gsize;
+      mb = r / gsize;
+    }
   }
 };
 

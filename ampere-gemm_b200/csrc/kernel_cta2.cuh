@@ -1,62 +1,75 @@
 // 2-CTA (cta_group::2) tcgen05 GEMM kernel: a cluster of two CTAs on two SMs
-// computes one 256 x 256 output tile with M=256, N=256 MMAs.
+// computes one (256 * MSUB) x 256 output tile with M=256, N=256 MMAs.
 //
-//   * CTA r of the pair loads A rows [m0 + 128 r, +128) and B columns
-//     [n0 + 128 r, +128) into its own shared memory (plain TMA, no multicast);
-//     the loads of both CTAs complete on the leader's (r = 0) full barrier.
-//   * The leader's MMA lane issues tcgen05.mma.cta_group::2, which reads A and
-//     B halves from both CTAs and writes rows [128 r, +128) of the fp32 tile
-//     into CTA r's TMEM.
+//   * CTA r of the pair owns MSUB blocks of 128 A rows,
+//     [m0 + 128 * (MSUB * r + s), +128) for s < MSUB, and B columns
+//     [n0 + 128 r, +128); it loads them into its own shared memory with plain
+//     TMA (no multicast).  The loads of both CTAs complete on the leader's
+//     (r = 0) full barrier.
+//   * Per 16-deep K step the leader issues MSUB MMAs of tcgen05.mma.cta_group::2:
+//     MMA s reads A block s of both CTAs and all 256 staged B columns and
+//     writes rows [128 r, +128) of its 256 x 256 fp32 result into CTA r's TMEM
+//     columns [256 s, +256).  With MSUB = 2 every staged B column feeds two
+//     MMAs, so a pair stages 25 % fewer bytes per FLOP than with MSUB = 1.
 //   * The leader frees a stage / publishes an accumulator with one
 //     tcgen05.commit per CTA (own barrier, then the peer's through mapa).
-//   * Each CTA's epilogue stores its own 128 rows; the peer's epilogue warps
-//     release the accumulator with a remote arrive on the leader's barrier.
-// Per SM this halves the B bytes staged per FLOP compared with the 1-CTA
-// 128 x 256 tile.  A stage holds KSUB 64-wide K slices: commits of a pair
-// reach their barriers late (about 1.6k cycles after issue), so a stage of
-// 8 MMAs (KSUB = 2) keeps the tensor pipe fed where 4 per stage does not.
+//   * Each CTA's epilogue stores its own rows; the peer's epilogue warps
+//     release accumulator space with remote arrives on the leader's barriers.
+//
+// TMEM (512 columns) holds two tiles' accumulators when MSUB = 1 (double
+// buffer: the epilogue of tile i overlaps the mainloop of tile i+1) and one
+// tile when MSUB = 2; then each 256-column half is released separately, so the
+// next tile's MMAs into the first half start while the second half drains.
+//
+// A stage holds KSUB 64-wide K slices.  Commits of a pair reach their barriers
+// late (about 1.6k cycles after issue), so a stage must carry at least 8 MMAs
+// (MSUB * KSUB * 4 >= 8) to keep the tensor pipe fed.
 #pragma once
 
 #include "gemm_common.cuh"
 
 namespace b200 {
 
-template <int STAGES, int KSUB>
+template <int STAGES, int KSUB, int MSUB>
 struct PairConfig {
   static constexpr int kStageK = kBK * KSUB;         // K per stage (KSUB swizzle atoms)
-  static constexpr int kTileM = 256;                 // rows per pair tile
+  static constexpr int kTileM = 256 * MSUB;          // rows per pair tile
   static constexpr int kTileN = 256;                 // columns per pair tile
   static constexpr int kHalfN = 128;                 // B columns staged per CTA
-  static constexpr int kASub = kBM * kBK * 2;       // 16 KB per 64-wide K slice of A
+  static constexpr int kASub = kBM * kBK * 2;        // 16 KB: 128 rows x 64 K of A
   static constexpr int kBSub = kHalfN * kBK * 2;     // 16 KB per 64-wide K slice of B (col-major B)
-  static constexpr int kABytes = kASub * KSUB;
+  static constexpr int kABytes = kASub * KSUB * MSUB;  // A stage: [msub][ksub] blocks
   static constexpr int kBBytes = kBSub * KSUB;
   static constexpr int kBPanel = kStageK * 128;      // row-major B: one 64-column panel of kStageK rows
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
-  static constexpr int kTmemCols = 2 * kTileN;       // two 256-column accumulators
+  static constexpr int kAccBufs = (MSUB == 1) ? 2 : 1;  // tiles resident in TMEM
+  static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 256 + 1024;
+  static_assert(kAccBufs * MSUB * kTileN <= kTmemCols, "accumulators exceed TMEM");
+  static_assert(MSUB * KSUB * (kBK / kUmmaK) >= 8, "a pair stage needs at least 8 MMAs");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int STAGES, int KSUB, bool kBRowMajor>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m) {
-  using Cfg = PairConfig<STAGES, KSUB>;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB>;
+  constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * Cfg::kABytes;
   uint8_t* smem_epi = smem + STAGES * Cfg::kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
-  uint64_t* full_bar = bars;                     // [STAGES] leader: both CTAs' loads landed
-  uint64_t* empty_bar = bars + STAGES;           // [STAGES] each CTA: its stage may be refilled
-  uint64_t* tmem_full = bars + 2 * STAGES;       // [2]      each CTA: accumulator ready
-  uint64_t* tmem_empty = bars + 2 * STAGES + 2;  // [2]      leader: both epilogues done reading
-  uint64_t* mma_drain = bars + 2 * STAGES + 4;   // [1]      abort path only
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* full_bar = bars;                          // [STAGES] leader: both CTAs' loads landed
+  uint64_t* empty_bar = bars + STAGES;                // [STAGES] each CTA: its stage may be refilled
+  uint64_t* tmem_full = bars + 2 * STAGES;            // [kAcc]   each CTA: a tile's accumulators ready
+  uint64_t* tmem_empty = bars + 2 * STAGES + kAcc;    // [kAcc * MSUB] leader: one 256-column block drained
+  uint64_t* mma_drain = tmem_empty + kAcc * MSUB;     // [1]      abort path only
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -81,10 +94,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 2 * kEpiWarps);
-    }
+    for (int a = 0; a < kAcc; ++a) mbar_init(&tmem_full[a], 1);
+    for (int a = 0; a < kAcc * MSUB; ++a) mbar_init(&tmem_empty[a], 2 * kEpiWarps);
     mbar_init(mma_drain, 1);
     fence_mbarrier_init();
   }
@@ -111,7 +122,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = pair; t < num_tiles && ok; t += num_pairs) {
         int mb, nb;
         sched.tile_coords(t, mb, nb);
-        const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * kBM;
+        const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * (kBM * MSUB);
         const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
@@ -124,11 +135,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kStageBytes);
           const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
           const int k0 = kb * Cfg::kStageK;
+          uint8_t* a_dst = smem_a + stage * Cfg::kABytes;
           uint8_t* b_dst = smem_b + stage * Cfg::kBBytes;
 #pragma unroll
-          for (int sub = 0; sub < KSUB; ++sub)
-            tma_load_2d_pair(smem_a + stage * Cfg::kABytes + sub * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
-                             m0, pol_a);
+          for (int s = 0; s < MSUB; ++s)
+#pragma unroll
+            for (int sub = 0; sub < KSUB; ++sub)
+              tma_load_2d_pair(a_dst + (s * KSUB + sub) * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
+                               m0 + kBM * s, pol_a);
           if constexpr (kBRowMajor) {
             // Panels of 64 columns x kStageK rows (one box each).
 #pragma unroll
@@ -156,8 +170,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA, one lane) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc =
-          make_idesc_f16_f32(Cfg::kTileM, Cfg::kTileN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
+      constexpr uint32_t idesc = make_idesc_f16_f32(256, Cfg::kTileN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
       const uint32_t a_base = smem_u32(smem_a);
       const uint32_t b_base = smem_u32(smem_b);
       int stage = 0;
@@ -169,12 +182,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const long long prof_t0 = clock64();
 #endif
       for (int t = pair; t < num_tiles && ok; t += num_pairs, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, kDevTimeoutMma))) { ok = false; break; }
-        tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kTileN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int buf = local % kAcc;
+        const uint32_t acc_phase = (local / kAcc) & 1;
+        for (int kb = 0; kb < num_kb && ok; ++kb) {
           if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
@@ -182,24 +192,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < Cfg::kStageK / kUmmaK; ++k) {
             const int sub = k / (kBK / kUmmaK), j = k % (kBK / kUmmaK);
-            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + sub * Cfg::kASub + j * (kUmmaK * 2));
             uint64_t bdesc;
             if constexpr (kBRowMajor)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), Cfg::kBPanel);
             else
               bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
+#pragma unroll
+            for (int s = 0; s < MSUB; ++s) {
+              if (kb == 0 && k == 0) {
+                // First write of this 256-column block in the tile: the
+                // epilogue must have drained it (both CTAs).
+                if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + s], acc_phase ^ 1u, kDevTimeoutMma))) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after_sync();
+              }
+              const uint64_t adesc = make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
+              const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
 #ifndef B200_GEMM_NOMMA
-            umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+              umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
 #endif
+              any_mma = true;
+            }
+            if (!ok) break;
           }
-          any_mma = true;
+          if (!ok) break;
           const uint32_t e = smem_u32(&empty_bar[stage]);
           umma_commit_cta2(e);
           umma_commit_cta2(mapa_shared(e, 1));
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        const uint32_t f = smem_u32(&tmem_full[acc]);
+        const uint32_t f = smem_u32(&tmem_full[buf]);
         umma_commit_cta2(f);
         umma_commit_cta2(mapa_shared(f, 1));
       }
@@ -215,60 +240,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     uint8_t* epi_buf = smem_epi + ew * 2 * kEpiBufBytes;
     const uint32_t epi_addr = smem_u32(epi_buf);
-    int buf = 0;
+    int sbuf = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += num_pairs, ++local) {
       int mb, nb;
       sched.tile_coords(t, mb, nb);
-      const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * kBM;
       const int n0 = nb * Cfg::kTileN;
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      // One lane per warp polls; the other 31 park at __syncwarp instead of
-      // hammering the barrier word in shared memory beside the tensor core.
+      const int buf = local % kAcc;
+      const uint32_t acc_phase = (local / kAcc) & 1;
       bool got = true;
-      if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[acc], acc_phase, kDevTimeoutEpilogue));
+      if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[buf], acc_phase, kDevTimeoutEpilogue));
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after_sync();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * Cfg::kTileN;
+#pragma unroll 1
+      for (int s = 0; s < MSUB; ++s) {
+        const int m0 = mb * Cfg::kTileM + (static_cast<int>(rank) * MSUB + s) * kBM;
+        const uint32_t t_row =
+            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + (buf * MSUB + s) * Cfg::kTileN;
 #ifdef B200_GEMM_NOEPI
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        if (true) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
-        else mbar_arrive(&tmem_empty[acc]);
-      }
-      continue;
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
+        continue;
 #endif
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
-        uint32_t lo[32], hi[32];
-        tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
-        tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
-        tmem_ld_wait_regs(lo);
-        tmem_ld_wait_regs(hi);
-        if (c == Cfg::kTileN / kEpiCols - 1) {
-          tc_fence_before_sync();
+        for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+          uint32_t lo[32], hi[32];
+          tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
+          tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
+          tmem_ld_wait_regs(lo);
+          tmem_ld_wait_regs(hi);
+          if (c == Cfg::kTileN / kEpiCols - 1) {
+            // This 256-column block is in registers: hand it back to the MMA warp.
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
+          }
+          if (lane == 0) bulk_wait_group_read<1>();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
-        }
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t row_addr = epi_addr + buf * kEpiBufBytes + lane * 128;
+          const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
-          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
-                       pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
+            st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
+                         pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_c, epi_buf + sbuf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
+            bulk_commit_group();
+          }
+          sbuf ^= 1;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_c, epi_buf + buf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
-          bulk_commit_group();
-        }
-        buf ^= 1;
       }
     }
     if (lane == 0) bulk_wait_group<0>();

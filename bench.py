@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 side measurements")
     ap.add_argument("--case", default=None,
                     help="single-GEMM mode for profiling/tuning: MxNxK[:colb] (1 GPU, not the driver line)")
-    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "skinny", "torch"],
+    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "skinny", "pair2m", "torch"],
                     help="kernel for --case (torch = torch.mm comparator)")
     ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"], help="inputs for --case")
     ap.add_argument("--graph", action="store_true", help="--case: time a CUDA-graph replay (device time only)")

@@ -121,6 +121,7 @@ B200_API int b200_gemm_sm_count(void);
 #define B200_VARIANT_CTA1 1 /* 1-CTA persistent kernel, 128 x 256 tiles */
 #define B200_VARIANT_PAIR 2 /* 2-CTA cluster (cta_group::2) kernel, 256 x 256 tiles */
 #define B200_VARIANT_SKINNY 3 /* K <= 256: B slice resident in shared memory, A streamed */
+#define B200_VARIANT_PAIR_WIDE 4 /* 2-CTA cluster kernel, 512 x 256 tiles (B reused by two MMAs) */
 
 /* Process-wide override of the kernel the library picks, for tests and
  * tuning; every variant computes the same product.  Returns

@@ -29,7 +29,7 @@ def _inputs(M, N, K, dev, dist="uniform", seed=0, std=1.0):
     return A.to(dev), B.to(dev)
 
 
-@pytest.fixture(params=["auto", "cta1", "pair", "skinny"])
+@pytest.fixture(params=["auto", "cta1", "pair", "skinny", "pair2m"])
 def variant(request, native_lib):
     _native.set_variant(request.param)
     yield request.param
