@@ -47,6 +47,7 @@ KERNEL_MODES = (
 )
 
 _MODE_TO_ID = {name: i for i, name in enumerate(KERNEL_MODES)}
+_F16 = torch.float16
 
 # Mode ids whose `gemm_pretransposed` operand is read as row-major K x N.  In
 # the reference, gemm_pretransposed(A, X, mode) with ids 2/3 called
@@ -99,9 +100,9 @@ def is_supported(A: torch.Tensor, B: torch.Tensor) -> bool:
         return False
     if A.shape[1] != B.shape[0]:
         return False
-    if A.dtype != torch.float16 or B.dtype != torch.float16:
+    if A.dtype != _F16 or B.dtype != _F16:
         return False
-    return A.device == B.device
+    return A.get_device() == B.get_device()
 
 
 def _check_operands(A: torch.Tensor, B: torch.Tensor) -> None:
@@ -122,11 +123,14 @@ def _check_operands(A: torch.Tensor, B: torch.Tensor) -> None:
         raise RuntimeError("A and B must be on the same CUDA device")
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_GET_DEVICE = getattr(torch._C, "_cuda_getDevice", None) or torch.cuda.current_device
+
+
 def _current_stream(dev: int) -> int:
     """Raw cudaStream_t of torch's current stream on `dev`."""
-    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
-    if raw is not None:
-        return raw(dev)
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(dev)
     return torch.cuda.current_stream(dev).cuda_stream
 
 
@@ -159,9 +163,9 @@ def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tens
     if M == 0 or N == 0:
         return C
     ldc = C.stride(0) if N > 1 else max(1, N)
-    dev = A.device.index
+    dev = A.get_device()
     layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
-    if dev != torch.cuda.current_device():
+    if dev != _GET_DEVICE():
         with torch.cuda.device(dev):
             code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev)
     else:
@@ -210,10 +214,11 @@ def gemm(A: torch.Tensor, B: torch.Tensor, mode: str = "wmma", out: torch.Tensor
     """C = A @ B with A M x K and B K x N (reference: gemm.py:219-228).
 
     Raises instead of falling back when ``is_supported`` is False.  ``out``
-    (optional, M x N fp16 CUDA, rows 16-byte aligned) receives the result
-    without a new allocation.
+    (optional, M x N fp16 CUDA tensor with unit column stride) receives the
+    result without a new allocation.
     """
-    _normalize_mode(mode)
+    if mode not in _MODE_TO_ID:
+        _normalize_mode(mode)
     if not is_supported(A, B):
         _check_operands(A, B)
         if A.shape[1] != B.shape[0]:
