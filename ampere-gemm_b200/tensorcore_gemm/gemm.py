@@ -136,14 +136,14 @@ def _current_stream(dev: int) -> int:
 
 def _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev) -> int:
     stream = _current_stream(dev)
-    if (K == 0 or (_tma_ok(A, lda) and _tma_ok(B, ldb))) and _tma_ok(C, ldc):
-        return _native.gemm_f16_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout, stream)
+    a, b, c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    if (K == 0 or (a % 16 == 0 and b % 16 == 0 and lda % 8 == 0 and ldb % 8 == 0)) and c % 16 == 0 and ldc % 8 == 0:
+        return _native.gemm_f16_raw(a, b, c, M, N, K, lda, ldb, ldc, layout, stream)
     # An operand TMA cannot address (odd K or N, or storage not 16-byte
     # aligned): the library re-pitches it through a workspace on the GPU.
-    ws_bytes = _native.workspace_size(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout)
+    ws_bytes = _native.workspace_size(a, b, c, M, N, K, lda, ldb, ldc, layout)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
-    return _native.gemm_f16_ws_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, ldb, ldc, layout,
-                                   ws.data_ptr(), ws_bytes, stream)
+    return _native.gemm_f16_ws_raw(a, b, c, M, N, K, lda, ldb, ldc, layout, ws.data_ptr(), ws_bytes, stream)
 
 
 def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tensor | None = None) -> torch.Tensor:

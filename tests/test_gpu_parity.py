@@ -256,3 +256,26 @@ def test_streamed_host_operands(cuda_device, native_lib, M, N, K, chunk):
     gemm_streamed(Ah, Bh.to(cuda_device), out=out, chunk_rows=chunk)
     torch.cuda.synchronize()
     assert torch.equal(out.cpu(), C)
+
+
+PARTIAL_WAVES = [(2048, 2048, 4096), (4096, 4096, 4096), (4000, 6000, 3000), (8192, 6144, 2048), (1536, 1280, 8192)]
+
+
+@pytest.mark.parametrize("M,N,K", PARTIAL_WAVES)
+@pytest.mark.parametrize("v", ["pair", "pair2m"])
+def test_pair_kernels_partial_last_wave(cuda_device, native_lib, M, N, K, v):
+    """Pair kernels on tile counts that leave the last wave partly idle:
+    within the bound, bit-identical run to run, equal in both B layouts."""
+    A, B = _inputs(M, N, K, cuda_device, dist="normal", seed=M + N)
+    _native.set_variant(v)
+    try:
+        C1 = tg.gemm(A, B)
+        C2 = tg.gemm(A, B)
+        C3 = tg.gemm_pretransposed(A, B.t().contiguous(), mode="reg_pingpong_256_colb")
+    finally:
+        _native.set_variant("auto")
+    torch.cuda.synchronize()
+    _no_device_error()
+    assert torch.equal(C1, C2)
+    assert torch.equal(C1, C3)
+    assert_parity(C1, fp32_ref(A, B), K, f"{v} {M}x{N}x{K}")
