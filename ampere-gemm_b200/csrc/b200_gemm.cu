@@ -28,6 +28,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "gemm_common.cuh"
 #include "kernel_cta1.cuh"
@@ -176,12 +177,38 @@ int ensure_smem_attr(Kern kern, int smem_bytes, std::atomic<uint8_t>* done) {
   return B200_OK;
 }
 
-template <int BN, int STAGES, bool kBRowMajor>
-int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
-                   int64_t ldc, int sm_count, int group_m, cudaStream_t stream) {
+// One GEMM call as the launchers see it (operands already TMA-compatible).
+struct GemmArgs {
+  const void* A;
+  const void* B;
+  void* C;
+  int M, N, K;
+  int64_t lda, ldb, ldc;
+  EpiScale scale;
+  int sm_count;
+  cudaStream_t stream;
+};
+
+// Calls fn(row-major B, column-major A) with the two layouts as compile-time
+// constants, so every launcher is instantiated for the four combinations.
+template <typename Fn>
+int with_layouts(bool row_b, bool col_a, Fn&& fn) {
+  if (row_b) return col_a ? fn(std::true_type{}, std::true_type{}) : fn(std::true_type{}, std::false_type{});
+  return col_a ? fn(std::false_type{}, std::true_type{}) : fn(std::false_type{}, std::false_type{});
+}
+
+template <int BN, int STAGES, bool kBRowMajor, bool kAColMajor>
+int launch_tcgen05(const GemmArgs& g, int group_m) {
   using Cfg = TileConfig<BN, STAGES>;
+  const void *A = g.A, *B = g.B;
+  void* C = g.C;
+  const int M = g.M, N = g.N, K = g.K;
+  const int64_t lda = g.lda, ldb = g.ldb, ldc = g.ldc;
+  const int sm_count = g.sm_count;
+  cudaStream_t stream = g.stream;
   CUtensorMap ta, tb, tc;
-  int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  int rc = kAColMajor ? make_tmap_2d(&ta, A, K, M, lda, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)
+                      : make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   if (kBRowMajor)
     rc = make_tmap_2d(&tb, B, K, N, ldb, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -191,12 +218,12 @@ int launch_tcgen05(const void* A, const void* B, void* C, int M, int N, int K, i
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
 
-  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, kBRowMajor>;
+  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, kBRowMajor, kAColMajor>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<long long>(tiles, sm_count);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m, g.scale);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -223,12 +250,18 @@ int max_active_pairs(Kern kern, int smem_bytes, int sm_count) {
   return n;
 }
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor>
-int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
-                        int64_t ldc, int sm_count, int group_m, cudaStream_t stream) {
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
+int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
+  const void *A = g.A, *B = g.B;
+  void* C = g.C;
+  const int M = g.M, N = g.N, K = g.K;
+  const int64_t lda = g.lda, ldb = g.ldb, ldc = g.ldc;
+  const int sm_count = g.sm_count;
+  cudaStream_t stream = g.stream;
   CUtensorMap ta, tb, tc;
-  int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  int rc = kAColMajor ? make_tmap_2d(&ta, A, K, M, lda, 64, Cfg::kStageK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)
+                      : make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   if (kBRowMajor)
     rc = make_tmap_2d(&tb, B, K, N, ldb, 64, Cfg::kStageK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -237,7 +270,7 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
@@ -251,7 +284,7 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
   }
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
-  kern<<<2 * grid_pairs, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m);
+  kern<<<2 * grid_pairs, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m, g.scale);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -259,14 +292,20 @@ int launch_tcgen05_pair(const void* A, const void* B, void* C, int M, int N, int
 // the number of 256-column N slices that fits the SMs, so every CTA keeps one
 // slice of B resident.  Returns B200_ERR_INVALID_ARGUMENT when the shape does
 // not qualify (caller falls back to another variant).
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor>
-int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc,
-                  int sm_count, cudaStream_t stream) {
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor>
+int launch_skinny(const GemmArgs& g) {
   using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
+  const void *A = g.A, *B = g.B;
+  void* C = g.C;
+  const int M = g.M, N = g.N, K = g.K;
+  const int64_t lda = g.lda, ldb = g.ldb, ldc = g.ldc;
+  const int sm_count = g.sm_count;
+  cudaStream_t stream = g.stream;
   const int num_nb = (N + Cfg::kBN - 1) / Cfg::kBN;
   if (K > Cfg::kMaxKBlocks * kBK || num_nb > sm_count) return B200_ERR_INVALID_ARGUMENT;
   CUtensorMap ta, tb, tc;
-  int rc = make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  int rc = kAColMajor ? make_tmap_2d(&ta, A, K, M, lda, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)
+                      : make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   if (kBRowMajor)
     rc = make_tmap_2d(&tb, B, K, N, ldb, 64, kBK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -275,13 +314,13 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor>;
+  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
   const int slots = (sm_count / num_nb) * num_nb;
   const int grid = (int)std::min<long long>(tiles, slots);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, g.scale);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -344,10 +383,11 @@ namespace {
 // Arguments common to every entry point.  Returns B200_OK, or an error code;
 // sets *nothing_to_do when the output is empty.
 int validate_args(const void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-                  int b_layout, const void* A, const void* B, bool* nothing_to_do) {
+                  int b_layout, const void* A, const void* B, bool* nothing_to_do, int a_layout = B200_A_ROW_MAJOR) {
   *nothing_to_do = false;
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   if (b_layout != B200_B_ROW_MAJOR && b_layout != B200_B_COL_MAJOR) return B200_ERR_INVALID_ARGUMENT;
+  if (a_layout != B200_A_ROW_MAJOR && a_layout != B200_A_COL_MAJOR) return B200_ERR_INVALID_ARGUMENT;
   const int64_t kMax = 0x7fffffff;
   if (M > kMax || N > kMax || K > kMax) return B200_ERR_TOO_LARGE;
   if (M == 0 || N == 0) {
@@ -357,22 +397,42 @@ int validate_args(const void* C, int64_t M, int64_t N, int64_t K, int64_t lda, i
   if (!C || ldc < N) return B200_ERR_INVALID_ARGUMENT;
   if (K > 0) {
     const bool row_b = (b_layout == B200_B_ROW_MAJOR);
-    if (!A || !B || lda < K || ldb < (row_b ? N : K)) return B200_ERR_INVALID_ARGUMENT;
+    const bool col_a = (a_layout == B200_A_COL_MAJOR);
+    if (!A || !B || lda < (col_a ? M : K) || ldb < (row_b ? N : K)) return B200_ERR_INVALID_ARGUMENT;
   }
   return B200_OK;
 }
 
 bool pitch_ok(const void* p, int64_t ld) { return aligned16(p) && (ld % 8) == 0; }
 
-// C = A * B on operands that already satisfy TMA's alignment rules.
+// C <- fp16_rn(beta * C) for an empty reduction (K == 0) with beta != 0.
+__global__ void scale_c_kernel(uint16_t* C, int64_t ldc, int64_t rows, int64_t cols, float beta) {
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += (int64_t)gridDim.x * blockDim.x) {
+      __half h = *reinterpret_cast<__half*>(&C[r * ldc + c]);
+      h = __float2half_rn(beta * __half2float(h));
+      C[r * ldc + c] = *reinterpret_cast<uint16_t*>(&h);
+    }
+}
+
+// C = alpha * op(A) * op(B) + beta * C on operands that already satisfy TMA's
+// alignment rules.
 int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                 int64_t ldc, int b_layout, const DeviceInfo& dev, cudaStream_t stream) {
+                 int64_t ldc, int a_layout, int b_layout, const EpiScale& scale, const DeviceInfo& dev,
+                 cudaStream_t stream) {
   if (K == 0) {
-    // Empty reduction: C is all zeros.
-    return cudaMemset2DAsync(C, ldc * 2, 0, N * 2, M, stream) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+    // Empty reduction: C = beta * C (all zeros when beta == 0).
+    if (scale.beta == 0.0f)
+      return cudaMemset2DAsync(C, ldc * 2, 0, N * 2, M, stream) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+    const unsigned gx = (unsigned)std::min<int64_t>((N + 255) / 256, 64);
+    const unsigned gy = (unsigned)std::min<int64_t>(M, 65535);
+    scale_c_kernel<<<dim3(gx, gy), 256, 0, stream>>>(static_cast<uint16_t*>(C), ldc, M, N, scale.beta);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+  const bool col_a = (a_layout == B200_A_COL_MAJOR);
   const int m = (int)M, n = (int)N, k = (int)K;
+  const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, scale, dev.sm_count, stream};
   int variant = g_variant;
   if (variant == B200_VARIANT_AUTO && k <= 256 && (n + 255) / 256 <= dev.sm_count) {
     // B-stationary pays for its one-off B load once a CTA has several tiles
@@ -382,8 +442,9 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   }
   if (variant == B200_VARIANT_AUTO) variant = pick_tensor_variant(m, n, k, dev.sm_count);
   if (variant == B200_VARIANT_SKINNY) {
-    const int rc = row_b ? launch_skinny<5, 1, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream)
-                         : launch_skinny<5, 1, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, stream);
+    const int rc = with_layouts(row_b, col_a, [&](auto rb, auto ca) {
+      return launch_skinny<5, 1, decltype(rb)::value, decltype(ca)::value>(g);
+    });
     if (rc != B200_ERR_INVALID_ARGUMENT) return rc;
     variant = B200_VARIANT_CTA1;  // shape outside the skinny kernel's range
   }
@@ -392,19 +453,20 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
     // Raster (measured DRAM bytes): when A is much taller than B is wide,
     // bands of 16 column blocks; otherwise bands of 8 row blocks.
     const int group_m = gm ? gm : (m >= 4LL * n ? -16 : 8);
-    if (row_b)
-      return launch_tcgen05_pair<4, 1, 2, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
-    return launch_tcgen05_pair<4, 1, 2, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
+      return launch_tcgen05_pair<4, 1, 2, decltype(rb)::value, decltype(ca)::value>(g, group_m);
+    });
   }
   if (variant == B200_VARIANT_PAIR) {
     const int group_m = gm ? gm : 8;  // 8 x 256-row bands: fewest DRAM bytes measured at 8192^3
-    if (row_b) return launch_tcgen05_pair<3, 2, 1, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
-    return launch_tcgen05_pair<3, 2, 1, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+    return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
+      return launch_tcgen05_pair<3, 2, 1, decltype(rb)::value, decltype(ca)::value>(g, group_m);
+    });
   }
   const int group_m = gm ? gm : 16;  // 16 x 128-row bands: fewest DRAM bytes measured at 8192^3
-  if (row_b)
-    return launch_tcgen05<256, 4, true>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
-  return launch_tcgen05<256, 4, false>(A, B, C, m, n, k, lda, ldb, ldc, dev.sm_count, group_m, stream);
+  return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
+    return launch_tcgen05<256, 4, decltype(rb)::value, decltype(ca)::value>(g, group_m);
+  });
 }
 
 // Copies a rows x cols fp16 matrix between row pitches (elements).
@@ -438,9 +500,10 @@ struct RepackPlan {
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 RepackPlan plan_repack(const void* A, const void* B, const void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                       int64_t ldb, int64_t ldc, int b_layout) {
+                       int64_t ldb, int64_t ldc, int b_layout, int a_layout = B200_A_ROW_MAJOR) {
   RepackPlan p;
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+  const bool col_a = (a_layout == B200_A_COL_MAJOR);
   if (K > 0) {
     p.a = !pitch_ok(A, lda);
     p.b = !pitch_ok(B, ldb);
@@ -448,9 +511,10 @@ RepackPlan plan_repack(const void* A, const void* B, const void* C, int64_t M, i
   p.c = !pitch_ok(C, ldc);
   int64_t off = 0;
   if (p.a) {
-    p.lda2 = round_up(K, 8);
+    const int64_t rows = col_a ? K : M, cols = col_a ? M : K;
+    p.lda2 = round_up(cols, 8);
     p.off_a = off;
-    off = round_up(off + M * p.lda2 * 2, 256);
+    off = round_up(off + rows * p.lda2 * 2, 256);
   }
   if (p.b) {
     const int64_t rows = row_b ? K : N, cols = row_b ? N : K;
@@ -470,9 +534,10 @@ RepackPlan plan_repack(const void* A, const void* B, const void* C, int64_t M, i
 // Repack (as planned), multiply, copy C back; `ws` is device memory of at
 // least plan.bytes, 256-byte aligned.
 int gemm_repacked(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                  int64_t ldc, int b_layout, const RepackPlan& p, uint8_t* ws, const DeviceInfo& dev,
-                  cudaStream_t stream) {
+                  int64_t ldc, int a_layout, int b_layout, const EpiScale& scale, const RepackPlan& p, uint8_t* ws,
+                  const DeviceInfo& dev, cudaStream_t stream) {
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
+  const bool col_a = (a_layout == B200_A_COL_MAJOR);
   const void* a = A;
   const void* b = B;
   void* c = C;
@@ -481,7 +546,7 @@ int gemm_repacked(const void* A, const void* B, void* C, int64_t M, int64_t N, i
   if (p.a) {
     a = ws + p.off_a;
     la = p.lda2;
-    if ((rc = pitched_copy(A, lda, ws + p.off_a, la, M, K, stream))) return rc;
+    if ((rc = pitched_copy(A, lda, ws + p.off_a, la, col_a ? K : M, col_a ? M : K, stream))) return rc;
   }
   if (p.b) {
     b = ws + p.off_b;
@@ -491,8 +556,9 @@ int gemm_repacked(const void* A, const void* B, void* C, int64_t M, int64_t N, i
   if (p.c) {
     c = ws + p.off_c;
     lc = p.ldc2;
+    if (scale.beta != 0.0f && (rc = pitched_copy(C, ldc, c, lc, M, N, stream))) return rc;  // old C is an input
   }
-  if ((rc = gemm_aligned(a, b, c, M, N, K, la, lb, lc, b_layout, dev, stream))) return rc;
+  if ((rc = gemm_aligned(a, b, c, M, N, K, la, lb, lc, a_layout, b_layout, scale, dev, stream))) return rc;
   if (p.c) rc = pitched_copy(c, lc, C, ldc, M, N, stream);
   return rc;
 }
@@ -511,35 +577,50 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
-  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, static_cast<cudaStream_t>(stream_ptr));
+  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, dev,
+                      static_cast<cudaStream_t>(stream_ptr));
+}
+
+extern "C" int64_t b200_gemm_workspace_size_ex(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                                               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int a_layout,
+                                               int b_layout) {
+  using namespace b200;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done, a_layout)) return -rc;
+  if (done) return 0;
+  return plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout, a_layout).bytes;
 }
 
 extern "C" int64_t b200_gemm_workspace_size(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                                             int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout) {
-  using namespace b200;
-  bool done = false;
-  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return -rc;
-  if (done) return 0;
-  return plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout).bytes;
+  return b200_gemm_workspace_size_ex(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout);
 }
 
-extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                                int64_t ldb, int64_t ldc, int b_layout, void* workspace, int64_t workspace_bytes,
-                                void* stream_ptr) {
+extern "C" int b200_gemm_f16_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                int64_t ldb, int64_t ldc, int a_layout, int b_layout, float alpha, float beta,
+                                void* workspace, int64_t workspace_bytes, void* stream_ptr) {
   using namespace b200;
   bool done = false;
-  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return rc;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done, a_layout)) return rc;
   if (done) return B200_OK;
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
-  if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, stream);
+  const EpiScale scale{alpha, beta};
+  const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout, a_layout);
+  if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, a_layout, b_layout, scale, dev, stream);
   if (!workspace || workspace_bytes < p.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return B200_ERR_WORKSPACE;
-  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, b_layout, p, static_cast<uint8_t*>(workspace), dev,
-                       stream);
+  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, a_layout, b_layout, scale, p,
+                       static_cast<uint8_t*>(workspace), dev, stream);
+}
+
+extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                int64_t ldb, int64_t ldc, int b_layout, void* workspace, int64_t workspace_bytes,
+                                void* stream_ptr) {
+  return b200_gemm_f16_ex(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, 1.0f, 0.0f, workspace,
+                          workspace_bytes, stream_ptr);
 }
 
 extern "C" int b200_gemm_set_variant(int variant) {
@@ -653,11 +734,13 @@ extern "C" int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int6
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
-  if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, b_layout, dev, stream);
+  if (p.bytes == 0)
+    return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, dev, stream);
   if (p.bytes > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
   uint8_t* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // Nothing in the scratch has to start at zero: the call writes every byte it
   // later reads (the re-pitched operand rows, and all of C's copy) first.
-  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, b_layout, p, scratch, dev, stream);
+  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, p, scratch, dev,
+                       stream);
 }

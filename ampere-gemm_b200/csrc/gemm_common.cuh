@@ -102,3 +102,75 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+// Epilogue scaling, the reference kernels' alpha / beta (tensorcore_gemm/
+// gemm.cu:1360-1364): C = fp16_rn(alpha * acc) when beta == 0, otherwise
+// C = fp16_rn(alpha * acc + beta * C_old), in fp32 with one rounding.
+struct EpiScale {
+  float alpha = 1.0f;
+  float beta = 0.0f;
+};
+
+// Writes one 32-row x 64-column block of C from the calling warp: lane l holds
+// row l's 64 fp32 values in lo (columns 0..31) and hi (32..63).  The block goes
+// through the warp's 128B-swizzled staging buffer (`NBUF` buffers, `sbuf`
+// rotates) and leaves with a TMA store at element (x, y) of C.  With beta != 0
+// the old C block is first brought into the same buffer by a TMA load that
+// completes on `cbar` (phase bit in `cphase`); the wait is bounded like every
+// other wait of the kernels.
+template <int NBUF>
+__device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8_t* epi_buf, uint32_t epi_addr,
+                                                int& sbuf, int lane, const uint32_t (&lo)[32],
+                                                const uint32_t (&hi)[32], int x, int y, const EpiScale& sc,
+                                                uint64_t* cbar, uint32_t& cphase) {
+  if (lane == 0) bulk_wait_group_read<NBUF - 1>();
+  __syncwarp();
+  uint8_t* buf = epi_buf + sbuf * kEpiBufBytes;
+  const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
+  bool have_old = false;
+  if (sc.beta != 0.0f) {
+    bool ok = true;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(cbar, kEpiBufBytes);
+      tma_load_2d(buf, tmap_c, cbar, x, y, policy_evict_first());
+      ok = mbar_wait(cbar, cphase, kDevTimeoutEpilogue);
+    }
+    cphase ^= 1u;
+    have_old = __shfl_sync(0xffffffffu, ok, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
+    const uint32_t addr = row_addr + ((j ^ (lane & 7)) << 4);
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = sc.alpha * __uint_as_float(v[e]);
+    if (have_old) {
+      uint32_t o[4];
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+                   : "r"(addr));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(&o[e]));
+        f[2 * e] = fmaf(sc.beta, old.x, f[2 * e]);
+        f[2 * e + 1] = fmaf(sc.beta, old.y, f[2 * e + 1]);
+      }
+    }
+    st_shared_v4(addr, pack_half2_rn(__float_as_uint(f[0]), __float_as_uint(f[1])),
+                 pack_half2_rn(__float_as_uint(f[2]), __float_as_uint(f[3])),
+                 pack_half2_rn(__float_as_uint(f[4]), __float_as_uint(f[5])),
+                 pack_half2_rn(__float_as_uint(f[6]), __float_as_uint(f[7])));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmap_c, buf, x, y);
+    bulk_commit_group();
+  }
+  sbuf = (sbuf + 1) % NBUF;
+}
+
+}  // namespace b200

@@ -5,10 +5,11 @@
 
 namespace b200 {
 
-template <int BN, int STAGES, bool kBRowMajor>
+template <int BN, int STAGES, bool kBRowMajor, bool kAColMajor>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m) {
+                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
+                            const EpiScale sc) {
   using Cfg = TileConfig<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -21,7 +22,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_full = bars + 2 * STAGES;      // [2]       MMA -> epilogue
   uint64_t* tmem_empty = bars + 2 * STAGES + 2; // [2]       epilogue -> MMA
   uint64_t* mma_drain = bars + 2 * STAGES + 4;  // [1]       abort path only
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* c_bar = bars + 2 * STAGES + 5;      // [4]       old-C loads of the epilogue warps (beta != 0)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -47,6 +49,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_empty[a], kEpiWarps);
     }
     mbar_init(mma_drain, 1);
+    for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -83,7 +86,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
           const int k0 = kb * kBK;
-          tma_load_2d(smem_a + stage * Cfg::kABytes, &tmap_a, &full_bar[stage], k0, m0, pol_a);
+          if constexpr (kAColMajor) {
+            // A stored K x M (M contiguous): two panels of 64 rows x 64 K.
+#pragma unroll
+            for (int p = 0; p < kBM / 64; ++p)
+              tma_load_2d(smem_a + stage * Cfg::kABytes + p * (kBK * 128), &tmap_a, &full_bar[stage], m0 + 64 * p, k0,
+                          pol_a);
+          } else {
+            tma_load_2d(smem_a + stage * Cfg::kABytes, &tmap_a, &full_bar[stage], k0, m0, pol_a);
+          }
           uint8_t* b_dst = smem_b + stage * Cfg::kBBytes;
           if constexpr (kBRowMajor) {
             // B is K x N with N contiguous: BN/64 panels of 64 columns x 64 K-rows.
@@ -113,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer (one lane) ----------------
     if (lane == 0) {
       constexpr uint32_t idesc =
-          make_idesc_f16_f32(kBM, BN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
+          make_idesc_f16_f32(kBM, BN, kAColMajor ? Major::kMN : Major::kK, kBRowMajor ? Major::kMN : Major::kK);
       const uint32_t a_base = smem_u32(smem_a);
       const uint32_t b_base = smem_u32(smem_b);
       int stage = 0;
@@ -137,7 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
+            const uint64_t adesc = kAColMajor ? make_desc_mnmajor_sw128(a_addr + k * (kUmmaK * 128), kBK * 128)
+                                              : make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
             uint64_t bdesc;
             if constexpr (kBRowMajor)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), kBK * 128);
@@ -167,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* epi_buf = smem_epi + ew * 2 * kEpiBufBytes;
     const uint32_t epi_addr = smem_u32(epi_buf);
     int buf = 0;
+    uint32_t c_phase = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
@@ -205,25 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
         // The store that last used this buffer must have finished reading it.
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t row_addr = epi_addr + buf * kEpiBufBytes + lane * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
-          const uint32_t p0 = pack_half2_rn(v[0], v[1]);
-          const uint32_t p1 = pack_half2_rn(v[2], v[3]);
-          const uint32_t p2 = pack_half2_rn(v[4], v[5]);
-          const uint32_t p3 = pack_half2_rn(v[6], v[7]);
-          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), p0, p1, p2, p3);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_c, epi_buf + buf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
-          bulk_commit_group();
-        }
-        buf ^= 1;
+        epi_store_block<2>(&tmap_c, epi_buf, epi_addr, buf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32, sc,
+                           &c_bar[ew], c_phase);
       }
     }
     if (lane == 0) bulk_wait_group<0>();

@@ -51,11 +51,12 @@ struct PairConfig {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
-                                 const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m) {
+                                 const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
+                                 const EpiScale sc) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
   constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -69,7 +70,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* tmem_full = bars + 2 * STAGES;            // [kAcc]   each CTA: a tile's accumulators ready
   uint64_t* tmem_empty = bars + 2 * STAGES + kAcc;    // [kAcc * MSUB] leader: one 256-column block drained
   uint64_t* mma_drain = tmem_empty + kAcc * MSUB;     // [1]      abort path only
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  uint64_t* c_bar = mma_drain + 1;                    // [4]      old-C loads of the epilogue warps (beta != 0)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(c_bar + kEpiWarps);
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -97,6 +99,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int a = 0; a < kAcc; ++a) mbar_init(&tmem_full[a], 1);
     for (int a = 0; a < kAcc * MSUB; ++a) mbar_init(&tmem_empty[a], 2 * kEpiWarps);
     mbar_init(mma_drain, 1);
+    for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -137,12 +140,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int k0 = kb * Cfg::kStageK;
           uint8_t* a_dst = smem_a + stage * Cfg::kABytes;
           uint8_t* b_dst = smem_b + stage * Cfg::kBBytes;
+          if constexpr (kAColMajor) {
+            // A stored K x M: each 128-row block is two panels of 64 rows x kStageK.
 #pragma unroll
-          for (int s = 0; s < MSUB; ++s)
+            for (int s = 0; s < MSUB; ++s)
 #pragma unroll
-            for (int sub = 0; sub < KSUB; ++sub)
-              tma_load_2d_pair(a_dst + (s * KSUB + sub) * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
-                               m0 + kBM * s, pol_a);
+              for (int p = 0; p < kBM / 64; ++p)
+                tma_load_2d_pair(a_dst + s * (Cfg::kASub * KSUB) + p * Cfg::kBPanel, &tmap_a, full_leader,
+                                 m0 + kBM * s + 64 * p, k0, pol_a);
+          } else {
+#pragma unroll
+            for (int s = 0; s < MSUB; ++s)
+#pragma unroll
+              for (int sub = 0; sub < KSUB; ++sub)
+                tma_load_2d_pair(a_dst + (s * KSUB + sub) * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
+                                 m0 + kBM * s, pol_a);
+          }
           if constexpr (kBRowMajor) {
             // Panels of 64 columns x kStageK rows (one box each).
 #pragma unroll
@@ -170,7 +183,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA, one lane) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16_f32(256, Cfg::kTileN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
+      constexpr uint32_t idesc = make_idesc_f16_f32(256, Cfg::kTileN, kAColMajor ? Major::kMN : Major::kK,
+                                                    kBRowMajor ? Major::kMN : Major::kK);
       const uint32_t a_base = smem_u32(smem_a);
       const uint32_t b_base = smem_u32(smem_b);
       int stage = 0;
@@ -208,7 +222,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after_sync();
               }
-              const uint64_t adesc = make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
+              const uint64_t adesc =
+                  kAColMajor
+                      ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
+                      : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
               const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
 #ifndef B200_GEMM_NOMMA
               umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
@@ -241,6 +258,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* epi_buf = smem_epi + ew * 2 * kEpiBufBytes;
     const uint32_t epi_addr = smem_u32(epi_buf);
     int sbuf = 0;
+    uint32_t c_phase = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += num_pairs, ++local) {
       int mb, nb;
@@ -277,22 +295,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
           }
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
-          const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
-            st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
-                         pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmap_c, epi_buf + sbuf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
-            bulk_commit_group();
-          }
-          sbuf ^= 1;
+          epi_store_block<2>(&tmap_c, epi_buf, epi_addr, sbuf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32, sc,
+                             &c_bar[ew], c_phase);
         }
       }
     }

@@ -35,10 +35,11 @@ struct SkinnyConfig {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor>
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                           const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K) {
+                           const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K,
+                           const EpiScale sc) {
   using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -52,7 +53,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_empty = bars + 2 * A_STAGES + 2;           // [2]
   uint64_t* b_full = bars + 2 * A_STAGES + 4;               // [4] B slice, one per 64-deep K block
   uint64_t* mma_drain = bars + 2 * A_STAGES + 8;            // [1] abort path only
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * A_STAGES + 9);
+  uint64_t* c_bar = bars + 2 * A_STAGES + 9;                // [4] old-C loads of the epilogue warps (beta != 0)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * A_STAGES + 13);
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -79,6 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int kb = 0; kb < Cfg::kMaxKBlocks; ++kb) mbar_init(&b_full[kb], 1);
     mbar_init(mma_drain, 1);
+    for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -117,7 +120,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::kABytes);
-          tma_load_2d(smem_a + stage * Cfg::kABytes, &tmap_a, &full_bar[stage], kb * kBK, m0, pol_a);
+          if constexpr (kAColMajor) {
+#pragma unroll
+            for (int p = 0; p < kBM / 64; ++p)
+              tma_load_2d(smem_a + stage * Cfg::kABytes + p * (kBK * 128), &tmap_a, &full_bar[stage], m0 + 64 * p,
+                          kb * kBK, pol_a);
+          } else {
+            tma_load_2d(smem_a + stage * Cfg::kABytes, &tmap_a, &full_bar[stage], kb * kBK, m0, pol_a);
+          }
           ++issued;
           if (++stage == A_STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -137,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc =
-          make_idesc_f16_f32(kBM, Cfg::kBN, Major::kK, kBRowMajor ? Major::kMN : Major::kK);
+          make_idesc_f16_f32(kBM, Cfg::kBN, kAColMajor ? Major::kMN : Major::kK, kBRowMajor ? Major::kMN : Major::kK);
       const uint32_t a_base = smem_u32(smem_a);
       const uint32_t b_base = smem_u32(smem_b);
       int stage = 0;
@@ -163,7 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = b_base + kb * Cfg::kBBlockBytes;
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            const uint64_t adesc = make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
+            const uint64_t adesc = kAColMajor ? make_desc_mnmajor_sw128(a_addr + k * (kUmmaK * 128), kBK * 128)
+                                              : make_desc_kmajor_sw128(a_addr + k * (kUmmaK * 2));
             uint64_t bdesc;
             if constexpr (kBRowMajor)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), kBK * 128);
@@ -192,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* epi_buf = smem_epi + ew * EPI_BUFS * kEpiBufBytes;
     const uint32_t epi_addr = smem_u32(epi_buf);
     int buf = 0;
+    uint32_t c_phase = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int m0 = (t / num_nb) * kBM;
@@ -215,22 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
-        if (lane == 0) bulk_wait_group_read<EPI_BUFS - 1>();
-        __syncwarp();
-        const uint32_t row_addr = epi_addr + buf * kEpiBufBytes + lane * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
-          st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
-                       pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_c, epi_buf + buf * kEpiBufBytes, n0 + c * kEpiCols, m0 + quad * 32);
-          bulk_commit_group();
-        }
-        buf = (buf + 1) % EPI_BUFS;
+        epi_store_block<EPI_BUFS>(&tmap_c, epi_buf, epi_addr, buf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32,
+                                  sc, &c_bar[ew], c_phase);
       }
     }
     if (lane == 0) bulk_wait_group<0>();

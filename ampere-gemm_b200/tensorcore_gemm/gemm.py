@@ -80,10 +80,6 @@ def _row_view(t: torch.Tensor) -> tuple[torch.Tensor, int]:
     return t, max(1, t.size(1))
 
 
-def _tma_ok(t: torch.Tensor, ld: int) -> bool:
-    return t.data_ptr() % 16 == 0 and ld % _ALIGN_ELEMS == 0
-
-
 def is_supported(A: torch.Tensor, B: torch.Tensor) -> bool:
     """True when ``gemm(A, B)`` runs on the B200 kernels.
 
@@ -134,30 +130,45 @@ def _current_stream(dev: int) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev) -> int:
+def _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev, a_layout=0, alpha=1.0, beta=0.0) -> int:
     stream = _current_stream(dev)
     a, b, c = A.data_ptr(), B.data_ptr(), C.data_ptr()
-    if (K == 0 or (a % 16 == 0 and b % 16 == 0 and lda % 8 == 0 and ldb % 8 == 0)) and c % 16 == 0 and ldc % 8 == 0:
+    aligned = (K == 0 or (a % 16 == 0 and b % 16 == 0 and lda % 8 == 0 and ldb % 8 == 0)) and \
+        c % 16 == 0 and ldc % 8 == 0
+    if aligned and a_layout == 0 and alpha == 1.0 and beta == 0.0:
         return _native.gemm_f16_raw(a, b, c, M, N, K, lda, ldb, ldc, layout, stream)
-    # An operand TMA cannot address (odd K or N, or storage not 16-byte
-    # aligned): the library re-pitches it through a workspace on the GPU.
-    ws_bytes = _native.workspace_size(a, b, c, M, N, K, lda, ldb, ldc, layout)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
-    return _native.gemm_f16_ws_raw(a, b, c, M, N, K, lda, ldb, ldc, layout, ws.data_ptr(), ws_bytes, stream)
+    ws_bytes = 0
+    ws_ptr = None
+    if not aligned:
+        # An operand TMA cannot address (odd K or N, or storage not 16-byte
+        # aligned): the library re-pitches it through a workspace on the GPU.
+        ws_bytes = _native.workspace_size_ex(a, b, c, M, N, K, lda, ldb, ldc, a_layout, layout)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=A.device)
+        ws_ptr = ws.data_ptr()
+    return _native.gemm_ex_raw(a, b, c, M, N, K, lda, ldb, ldc, a_layout, layout, alpha, beta, ws_ptr, ws_bytes,
+                               stream)
 
 
-def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tensor | None = None) -> torch.Tensor:
-    """C = A @ B (B given as K x N) or A @ B.T (B given as N x K, b_col_major)."""
+def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tensor | None = None,
+            alpha: float = 1.0, beta: float = 0.0) -> torch.Tensor:
+    """C = alpha * A @ B + beta * out (B given as K x N, or as N x K when b_col_major)."""
     M, K = A.shape
     N = B.shape[0] if b_col_major else B.shape[1]
     if not b_col_major and B.stride(0) == 1 and B.stride(1) >= max(1, K) and B.size(0) > 1:
         # B is the transpose view of an N x K row-major buffer: read it as colb.
         B = B.t()
         b_col_major = True
-    A, lda = _row_view(A)
+    a_layout = _native.B200_A_ROW_MAJOR
+    if A.stride(0) == 1 and A.stride(1) >= max(1, M) and A.size(1) > 1 and A.size(0) > 1:
+        # A is the transpose view of a K x M row-major buffer: read it in place.
+        a_layout = _native.B200_A_COL_MAJOR
+        lda = A.stride(1)
+    else:
+        A, lda = _row_view(A)
     B, ldb = _row_view(B)
     if out is None:
         C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+        beta = 0.0
     else:
         C = out
     if M == 0 or N == 0:
@@ -167,9 +178,9 @@ def _launch(A: torch.Tensor, B: torch.Tensor, b_col_major: bool, out: torch.Tens
     layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
     if dev != _GET_DEVICE():
         with torch.cuda.device(dev):
-            code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev)
+            code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev, a_layout, alpha, beta)
     else:
-        code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev)
+        code = _call(A, B, C, M, N, K, lda, ldb, ldc, layout, dev, a_layout, alpha, beta)
     _native.check(code, "root_gemm launch")
     return C
 
@@ -229,3 +240,23 @@ def gemm(A: torch.Tensor, B: torch.Tensor, mode: str = "wmma", out: torch.Tensor
                 or (out.shape[1] > 1 and out.stride(1) != 1)):
             raise RuntimeError("out must be an M x N float16 tensor on A's device with unit column stride")
     return _launch(A, B, False, out)
+
+
+def gemm_ex(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+            beta: float = 0.0) -> torch.Tensor:
+    """C = alpha * A @ B + beta * out, the reference kernels' alpha / beta
+    epilogue (gemm.cu:1360-1364), which the reference launcher fixed to 1 / 0.
+
+    A and B may be row-major or transpose views (read in place).  With
+    beta != 0, `out` must be given and holds the old C on entry.
+    """
+    if not is_supported(A, B):
+        _check_operands(A, B)
+        raise RuntimeError("Inner dimensions must match")
+    if beta != 0.0 and out is None:
+        raise RuntimeError("beta != 0 needs `out` holding the old C")
+    if out is not None:
+        if (out.dtype != torch.float16 or out.device != A.device or tuple(out.shape) != (A.shape[0], B.shape[1])
+                or (out.shape[1] > 1 and out.stride(1) != 1)):
+            raise RuntimeError("out must be an M x N float16 tensor on A's device with unit column stride")
+    return _launch(A, B, False, out, float(alpha), float(beta))

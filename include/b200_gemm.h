@@ -37,6 +37,9 @@ extern "C" {
 #define B200_B_ROW_MAJOR 0
 #define B200_B_COL_MAJOR 1
 
+#define B200_A_ROW_MAJOR 0 /* A stored M x K, element (i, k) at A[i * lda + k] */
+#define B200_A_COL_MAJOR 1 /* A stored K x M, element (i, k) at A[k * lda + i] */
+
 /* Return codes. */
 #define B200_OK 0
 #define B200_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad layout, ld too small */
@@ -102,6 +105,24 @@ B200_API int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, 
  */
 B200_API int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                                    int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* stream);
+
+/*
+ * General form: C = alpha * A * B + beta * C, with either layout for A and
+ * for B, and an optional workspace for operands TMA cannot address (sized by
+ * b200_gemm_workspace_size_ex; NULL / 0 when none is needed).  alpha and beta
+ * are the reference kernels' epilogue parameters (tensorcore_gemm/gemm.cu
+ * :1073 signature, epilogue :1360-1364: fp16_rn(alpha * acc) when beta == 0,
+ * else fp16_rn(alpha * acc + beta * C_old)); the reference launcher fixed them
+ * to 1 and 0 (gemm.py:87).  A column-major A (a transposed view of a K x M
+ * buffer) is read in place; the reference made such inputs contiguous first
+ * (gemm.py:213-225).  With beta != 0, C must hold the old values on entry.
+ */
+B200_API int b200_gemm_f16_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                              int64_t ldb, int64_t ldc, int a_layout, int b_layout, float alpha, float beta,
+                              void* workspace, int64_t workspace_bytes, void* stream);
+B200_API int64_t b200_gemm_workspace_size_ex(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                                             int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int a_layout,
+                                             int b_layout);
 
 /* Human-readable text of a return code (static storage). Counterpart of the
  * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */

@@ -279,3 +279,72 @@ def test_pair_kernels_partial_last_wave(cuda_device, native_lib, M, N, K, v):
     assert torch.equal(C1, C2)
     assert torch.equal(C1, C3)
     assert_parity(C1, fp32_ref(A, B), K, f"{v} {M}x{N}x{K}")
+
+
+COLA = [(300, 264, 200), (1024, 512, 2048), (4096, 4096, 1024), (32768, 1024, 256), (129, 136, 72)]
+
+
+@pytest.mark.parametrize("M,N,K", COLA)
+@pytest.mark.parametrize("colb", [False, True])
+def test_column_major_a_in_place(cuda_device, variant, M, N, K, colb):
+    """A given as the transpose view of a K x M buffer is read without a copy."""
+    A, B = _inputs(M, N, K, cuda_device, dist="normal", seed=M + 2 * N + K)
+    At = A.t().contiguous()           # K x M storage
+    Aview = At.t()                    # M x K, column-major
+    assert Aview.stride(0) == 1
+    if colb:
+        C = tg.gemm_pretransposed(Aview, B.t().contiguous(), mode="reg_pingpong_256_colb")
+    else:
+        C = tg.gemm(Aview, B)
+    torch.cuda.synchronize()
+    _no_device_error()
+    assert torch.equal(C, tg.gemm(A, B)), "column-major A must give the row-major result bit for bit"
+    assert_parity(C, fp32_ref(A, B), K)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 320), (4096, 4096, 4096), (32768, 1024, 256), (37, 24, 40)])
+@pytest.mark.parametrize("alpha,beta", [(0.5, 0.0), (1.0, 1.0), (-2.0, 0.25), (0.0, 3.0)])
+def test_alpha_beta_epilogue(cuda_device, variant, M, N, K, alpha, beta):
+    gemm_ex = gemm_mod.gemm_ex
+    A, B = _inputs(M, N, K, cuda_device, dist="normal", seed=M + K)
+    C0 = (torch.randn((M, N), device=cuda_device) * 4).half()
+    out = C0.clone()
+    gemm_ex(A, B, out=out, alpha=alpha, beta=beta)
+    torch.cuda.synchronize()
+    _no_device_error()
+    ref = alpha * fp32_ref(A, B) + beta * C0.float()
+    assert_parity(out, ref, K, f"alpha={alpha} beta={beta}")
+
+
+def test_alpha_beta_odd_output_pitch_and_empty_k(cuda_device, native_lib):
+    gemm_ex = gemm_mod.gemm_ex
+    M, N, K = 100, 37, 72                 # N odd: C goes through the re-pitch workspace
+    A, B = _inputs(M, N, K, cuda_device, seed=3)
+    C0 = torch.randn((M, N), device=cuda_device).half()
+    out = C0.clone()
+    gemm_ex(A, B, out=out, alpha=1.5, beta=-0.5)
+    assert_parity(out, 1.5 * fp32_ref(A, B) + (-0.5) * C0.float(), K)
+    E = torch.empty((M, 0), dtype=torch.float16, device=cuda_device)
+    F = torch.empty((0, N), dtype=torch.float16, device=cuda_device)
+    out2 = C0.clone()
+    gemm_ex(E, F, out=out2, alpha=1.0, beta=2.0)  # K = 0: C = 2 C
+    torch.cuda.synchronize()
+    assert torch.equal(out2, (2.0 * C0.float()).half())
+
+
+def test_column_major_a_odd_pitch_abi(cuda_device, native_lib):
+    """C ABI: column-major A whose pitch is odd goes through the workspace."""
+    M, N, K = 203, 64, 96
+    A, B = _inputs(M, N, K, cuda_device, seed=8)
+    buf = torch.zeros((K, M + 3), dtype=torch.float16, device=cuda_device)   # lda = M + 3 (odd)
+    buf[:, :M] = A.t()
+    C = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    args = (buf.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, M + 3, N, N,
+            _native.B200_A_COL_MAJOR, _native.B200_B_ROW_MAJOR)
+    need = _native.workspace_size_ex(*args)
+    assert need > 0
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    rc = _native.gemm_ex_raw(*args, 1.0, 0.0, ws.data_ptr(), need, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert_parity(C, fp32_ref(A, B), K)
