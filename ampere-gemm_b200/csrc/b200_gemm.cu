@@ -187,6 +187,7 @@ struct GemmArgs {
   EpiScale scale;
   int sm_count;
   cudaStream_t stream;
+  ArgminOut argmin = ArgminOut{};
 };
 
 // Calls fn(row-major B, column-major A) with the two layouts as compile-time
@@ -292,7 +293,7 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
 // the number of 256-column N slices that fits the SMs, so every CTA keeps one
 // slice of B resident.  Returns B200_ERR_INVALID_ARGUMENT when the shape does
 // not qualify (caller falls back to another variant).
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor>
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false>
 int launch_skinny(const GemmArgs& g) {
   using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
   const void *A = g.A, *B = g.B;
@@ -312,15 +313,18 @@ int launch_skinny(const GemmArgs& g) {
   else
     rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, Cfg::kBN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
-  rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  if constexpr (kArgmin)
+    tc = ta;  // no C: the argmin epilogue writes keys, the map is never used
+  else
+    rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor>;
+  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor, kArgmin>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
   const int slots = (sm_count / num_nb) * num_nb;
   const int grid = (int)std::min<long long>(tiles, slots);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, g.scale);
+  kern<<<grid, kArgmin ? 320 : kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, g.scale, g.argmin);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -743,4 +747,96 @@ extern "C" int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int6
   // later reads (the re-pitched operand rows, and all of C's copy) first.
   return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, p, scratch, dev,
                        stream);
+}
+
+// ===========================================================================
+// K-means assignment (b200_kmeans_assign_f16)
+// ===========================================================================
+namespace b200 {
+namespace {
+
+// ||c_j||^2 in fp32 for each centroid j (column j of a row-major K x N matrix,
+// or row j of an N x K one).
+__global__ void centroid_norms_kernel(const __half* Cent, int64_t ld, int N, int K, int row_major_kn, float* out) {
+  if (row_major_kn) {
+    // Column j of K x N: consecutive threads read consecutive columns.
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= N) return;
+    float s = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float v = __half2float(Cent[(int64_t)k * ld + j]);
+      s = fmaf(v, v, s);
+    }
+    out[j] = s;
+  } else {
+    // Row j of N x K: one warp per centroid, lanes stride along the row.
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (j >= N) return;
+    float s = 0.0f;
+    for (int k = lane; k < K; k += 32) {
+      const float v = __half2float(Cent[(int64_t)j * ld + k]);
+      s = fmaf(v, v, s);
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[j] = s;
+  }
+}
+
+__global__ void unpack_keys_kernel(const unsigned long long* keys, int M, int* idx, float* score) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M) return;
+  const unsigned long long k = keys[i];
+  idx[i] = (int)(k & 0xffffffffu);
+  if (score) score[i] = ordered_to_float((uint32_t)(k >> 32));
+}
+
+int64_t kmeans_ws_parts(int64_t M, int64_t N, int64_t* keys_off) {
+  *keys_off = round_up(N * 4, 256);
+  return *keys_off + round_up(M * 8, 256);
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int64_t b200_kmeans_workspace_size(int64_t M, int64_t N) {
+  if (M < 0 || N < 0) return -B200_ERR_INVALID_ARGUMENT;
+  int64_t off = 0;
+  return b200::kmeans_ws_parts(M, N, &off);
+}
+
+extern "C" int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                      int64_t ldcent, int cent_layout, void* workspace, int64_t workspace_bytes,
+                                      int32_t* out_idx, float* out_score, void* stream_ptr) {
+  using namespace b200;
+  if (M < 0 || N <= 0 || K <= 0 || K > 256) return K > 256 ? B200_ERR_TOO_LARGE : B200_ERR_INVALID_ARGUMENT;
+  if (cent_layout != B200_B_ROW_MAJOR && cent_layout != B200_B_COL_MAJOR) return B200_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || N > 0x7fffffff) return B200_ERR_TOO_LARGE;
+  if (M == 0) return B200_OK;
+  const bool row_b = (cent_layout == B200_B_ROW_MAJOR);
+  if (!X || !Cent || !out_idx || ldx < K || ldcent < (row_b ? N : K)) return B200_ERR_INVALID_ARGUMENT;
+  if (!pitch_ok(X, ldx) || !pitch_ok(Cent, ldcent)) return B200_ERR_MISALIGNED;
+  int64_t keys_off = 0;
+  const int64_t need = kmeans_ws_parts(M, N, &keys_off);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return B200_ERR_WORKSPACE;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  if ((N + 255) / 256 > dev.sm_count) return B200_ERR_TOO_LARGE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  float* cnorm = static_cast<float*>(workspace);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + keys_off);
+  const unsigned norm_blocks = row_b ? (unsigned)((N + 127) / 128) : (unsigned)((N * 32 + 127) / 128);
+  centroid_norms_kernel<<<norm_blocks, 128, 0, stream>>>(static_cast<const __half*>(Cent), ldcent, (int)N, (int)K,
+                                                          row_b ? 1 : 0, cnorm);
+  if (cudaGetLastError() != cudaSuccess) return B200_ERR_CUDA;
+  if (cudaMemsetAsync(keys, 0xff, M * 8, stream) != cudaSuccess) return B200_ERR_CUDA;
+  GemmArgs g{X, Cent, nullptr, (int)M, (int)N, (int)K, ldx, ldcent, 0, EpiScale{}, dev.sm_count, stream};
+  g.argmin.cnorm = cnorm;
+  g.argmin.keys = keys;
+  const int rc = row_b ? launch_skinny<5, 1, true, false, true>(g) : launch_skinny<5, 1, false, false, true>(g);
+  if (rc) return rc;
+  unpack_keys_kernel<<<(unsigned)((M + 255) / 256), 256, 0, stream>>>(keys, (int)M, out_idx, out_score);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }

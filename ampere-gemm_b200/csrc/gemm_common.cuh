@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cstdint>
+#include <cstring>
 
 #include "sm100_ptx.cuh"
 #include "umma_desc.h"
@@ -171,6 +172,34 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
     bulk_commit_group();
   }
   sbuf = (sbuf + 1) % NBUF;
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+// K-means assignment fused into the epilogue: for every row i of A (a point)
+// the kernel keeps min_j (cnorm[j] - 2 * acc[i][j]) over its N slice and
+// merges slices with a 64-bit atomicMin on `keys[i]` (score in the high 32
+// bits as an order-preserving integer, column index in the low 32 bits, so
+// equal scores resolve to the smaller index whatever the order of arrival).
+// keys must hold ~0ull on entry.
+struct ArgminOut {
+  const float* cnorm = nullptr;          // ||c_j||^2, N entries
+  unsigned long long* keys = nullptr;    // M entries
+};
+
+__host__ __device__ __forceinline__ uint32_t float_to_ordered(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__host__ __device__ __forceinline__ float ordered_to_float(uint32_t u) {
+  u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
 }
 
 }  // namespace b200

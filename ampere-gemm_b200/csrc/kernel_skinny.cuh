@@ -31,22 +31,28 @@ struct SkinnyConfig {
   static constexpr int kBBytes = kMaxKBlocks * kBBlockBytes;
   static constexpr int kEpiBytes = kEpiWarps * EPI_BUFS * kEpiBufBytes;
   static constexpr int kTmemCols = 2 * kBN;
-  static constexpr int kSmemBytes = kBBytes + A_STAGES * kABytes + kEpiBytes + 256 + 1024;
+  static constexpr int kNormBytes = kBN * 4;                // argmin mode: the CTA's slice of ||c||^2
+  static constexpr int kSmemBytes = kBBytes + A_STAGES * kABytes + kEpiBytes + kNormBytes + 256 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false>
+__global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
     gemm_f16_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K,
-                           const EpiScale sc) {
+                           const EpiScale sc, const ArgminOut am = ArgminOut{}) {
   using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
+  // The argmin epilogue is instruction-bound, so it runs on 8 warps (two per
+  // TMEM lane quadrant, each on half of the columns); the store epilogue
+  // keeps 4 (its staging buffers would not fit twice).
+  constexpr int kEpiW = kArgmin ? 8 : kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_b = smem;                                   // resident B slice
   uint8_t* smem_a = smem + Cfg::kBBytes;                    // A ring
   uint8_t* smem_epi = smem_a + A_STAGES * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
+  float* s_norm = reinterpret_cast<float*>(smem_epi + Cfg::kEpiBytes);   // [kBN], argmin mode
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes + Cfg::kNormBytes);
   uint64_t* full_bar = bars;                                // [A_STAGES]
   uint64_t* empty_bar = bars + A_STAGES;                    // [A_STAGES]
   uint64_t* tmem_full = bars + 2 * A_STAGES;                // [2]
@@ -77,7 +83,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], kEpiWarps);
+      mbar_init(&tmem_empty[a], kEpiW);
     }
     for (int kb = 0; kb < Cfg::kMaxKBlocks; ++kb) mbar_init(&b_full[kb], 1);
     mbar_init(mma_drain, 1);
@@ -200,11 +206,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue warps 2..5 ----------------
     const int quad = warp & 3;
     const int ew = warp - 2;
+    constexpr int kChunksPerWarp = (Cfg::kBN / kEpiCols) * kEpiWarps / kEpiW;
+    const int c_begin = (ew / kEpiWarps) * kChunksPerWarp;
+    const int c_end = c_begin + kChunksPerWarp;
     uint8_t* epi_buf = smem_epi + ew * EPI_BUFS * kEpiBufBytes;
     const uint32_t epi_addr = smem_u32(epi_buf);
     int buf = 0;
     uint32_t c_phase = 0;
     int local = 0;
+    if constexpr (kArgmin) {
+      // This CTA's N slice never changes: stage its norms once (+inf past N,
+      // so those columns never win), then sync the four epilogue warps.
+      for (int j = threadIdx.x - 64; j < Cfg::kBN; j += kEpiW * 32)
+        s_norm[j] = (n0 + j < N) ? am.cnorm[n0 + j] : __int_as_float(0x7f800000);
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiW * 32) : "memory");
+    }
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int m0 = (t / num_nb) * kBM;
       const int acc = local & 1;
@@ -215,20 +231,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!got) break;
       tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * Cfg::kBN;
+      float best_d = __int_as_float(0x7f800000);  // +inf
+      int best_i = 0x7fffffff;
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kBN / kEpiCols; ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
         uint32_t lo[32], hi[32];
         tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
         tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
         tmem_ld_wait_regs(lo);
         tmem_ld_wait_regs(hi);
-        if (c == Cfg::kBN / kEpiCols - 1) {
+        if (c == c_end - 1) {
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tmem_empty[acc]);
         }
+        if constexpr (kArgmin) {
+          // Scores of this 64-column chunk, their minimum, then the first
+          // column reaching it (smallest index on ties).
+          float d[kEpiCols];
+          const float4* nrm = reinterpret_cast<const float4*>(s_norm + c * kEpiCols);
+#pragma unroll
+          for (int q = 0; q < kEpiCols / 4; ++q) {
+            const float4 v = nrm[q];
+            const float nv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int e = 4 * q + t;
+              d[e] = fmaf(-2.0f, __uint_as_float(e < 32 ? lo[e] : hi[e - 32]), nv[t]);
+            }
+          }
+          float m = d[0];
+#pragma unroll
+          for (int e = 1; e < kEpiCols; ++e) m = fminf(m, d[e]);
+          if (m < best_d) {
+            int first = kEpiCols - 1;
+#pragma unroll
+            for (int e = kEpiCols - 1; e >= 0; --e)
+              if (d[e] == m) first = e;
+            best_d = m;
+            best_i = n0 + c * kEpiCols + first;
+          }
+          continue;
+        }
         epi_store_block<EPI_BUFS>(&tmap_c, epi_buf, epi_addr, buf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32,
                                   sc, &c_bar[ew], c_phase);
+      }
+      if constexpr (kArgmin) {
+        const int row = m0 + quad * 32 + lane;
+        if (row < M && best_i != 0x7fffffff)
+          atomicMin(am.keys + row, ((unsigned long long)float_to_ordered(best_d) << 32) | (unsigned)best_i);
       }
     }
     if (lane == 0) bulk_wait_group<0>();

@@ -124,6 +124,24 @@ B200_API int64_t b200_gemm_workspace_size_ex(const void* A, const void* B, const
                                              int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int a_layout,
                                              int b_layout);
 
+/*
+ * K-means assignment fused into the skinny GEMM (the consumer the reference's
+ * K = 256 "K-means-like" shapes stand for, README.md:44): for every point
+ * (row of X, M x K) the index of the centroid minimising
+ * score_j = ||c_j||^2 - 2 x . c_j  (= ||x - c_j||^2 - ||x||^2), without
+ * writing the M x N product.  Centroids are K x N row-major
+ * (cent_layout = B200_B_ROW_MAJOR) or stored N x K (B200_B_COL_MAJOR).
+ * 1 <= K <= 256; X and Cent TMA-compatible (16-byte bases, pitches multiple
+ * of 8).  Ties go to the smaller index.  out_score (optional) receives the
+ * winning score.  The workspace (b200_kmeans_workspace_size bytes, 256-byte
+ * aligned) holds the centroid norms and per-point keys.  No counterpart in
+ * the reference, which stops at the GEMM.
+ */
+B200_API int64_t b200_kmeans_workspace_size(int64_t M, int64_t N);
+B200_API int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                    int64_t ldcent, int cent_layout, void* workspace, int64_t workspace_bytes,
+                                    int32_t* out_idx, float* out_score, void* stream);
+
 /* Human-readable text of a return code (static storage). Counterpart of the
  * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */
 B200_API const char* b200_gemm_strerror(int code);
