@@ -184,11 +184,15 @@ struct GemmArgs {
   void* C;
   int M, N, K;
   int64_t lda, ldb, ldc;
-  EpiScale scale;
+  EpiParams scale;
   int sm_count;
   cudaStream_t stream;
   ArgminOut argmin = ArgminOut{};
 };
+
+// Width of C's tensor map: the columns the TMA store covers (at least one
+// column so the map encodes; when N < 8 it is never used).
+inline int c_map_cols(const GemmArgs& g) { return g.scale.n_tma > 0 ? g.scale.n_tma : g.N; }
 
 // Calls fn(row-major B, column-major A) with the two layouts as compile-time
 // constants, so every launcher is instantiated for the four combinations.
@@ -216,7 +220,7 @@ int launch_tcgen05(const GemmArgs& g, int group_m) {
   else
     rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, BN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
-  rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
 
   auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, kBRowMajor, kAColMajor>;
@@ -269,7 +273,7 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   else
     rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, Cfg::kHalfN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
-  rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
   auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
@@ -316,7 +320,7 @@ int launch_skinny(const GemmArgs& g) {
   if constexpr (kArgmin)
     tc = ta;  // no C: the argmin epilogue writes keys, the map is never used
   else
-    rc = make_tmap_2d(&tc, C, M, N, ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
   auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor, kArgmin>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
@@ -422,7 +426,7 @@ __global__ void scale_c_kernel(uint16_t* C, int64_t ldc, int64_t rows, int64_t c
 // C = alpha * op(A) * op(B) + beta * C on operands that already satisfy TMA's
 // alignment rules.
 int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                 int64_t ldc, int a_layout, int b_layout, const EpiScale& scale, const DeviceInfo& dev,
+                 int64_t ldc, int a_layout, int b_layout, const EpiParams& scale, const DeviceInfo& dev,
                  cudaStream_t stream) {
   if (K == 0) {
     // Empty reduction: C = beta * C (all zeros when beta == 0).
@@ -436,7 +440,13 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
   const bool col_a = (a_layout == B200_A_COL_MAJOR);
   const int m = (int)M, n = (int)N, k = (int)K;
-  const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, scale, dev.sm_count, stream};
+  EpiParams ep = scale;
+  ep.m = m;
+  ep.n = n;
+  ep.ldc = ldc;
+  ep.c = static_cast<uint16_t*>(C);
+  ep.n_tma = n & ~7;  // a TMA store writes whole 16-byte pieces: the partial last one goes by plain stores
+  const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, ep, dev.sm_count, stream};
   int variant = g_variant;
   if (variant == B200_VARIANT_AUTO && k <= 256 && (n + 255) / 256 <= dev.sm_count) {
     // B-stationary pays for its one-off B load once a CTA has several tiles
@@ -538,7 +548,7 @@ RepackPlan plan_repack(const void* A, const void* B, const void* C, int64_t M, i
 // Repack (as planned), multiply, copy C back; `ws` is device memory of at
 // least plan.bytes, 256-byte aligned.
 int gemm_repacked(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                  int64_t ldc, int a_layout, int b_layout, const EpiScale& scale, const RepackPlan& p, uint8_t* ws,
+                  int64_t ldc, int a_layout, int b_layout, const EpiParams& scale, const RepackPlan& p, uint8_t* ws,
                   const DeviceInfo& dev, cudaStream_t stream) {
   const bool row_b = (b_layout == B200_B_ROW_MAJOR);
   const bool col_a = (a_layout == B200_A_COL_MAJOR);
@@ -581,7 +591,7 @@ extern "C" int b200_gemm_f16(const void* A, const void* B, void* C, int64_t M, i
   DeviceInfo dev;
   if (int rc = current_device_info(dev)) return rc;
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
-  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, dev,
+  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiParams{}, dev,
                       static_cast<cudaStream_t>(stream_ptr));
 }
 
@@ -611,7 +621,7 @@ extern "C" int b200_gemm_f16_ex(const void* A, const void* B, void* C, int64_t M
   if (int rc = current_device_info(dev)) return rc;
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const EpiScale scale{alpha, beta};
+  const EpiParams scale{alpha, beta};
   const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout, a_layout);
   if (p.bytes == 0) return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, a_layout, b_layout, scale, dev, stream);
   if (!workspace || workspace_bytes < p.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
@@ -664,7 +674,7 @@ extern "C" int b200_gemm_sm_count(void) {
   return d.sm_count;
 }
 
-extern "C" int b200_gemm_version(void) { return 100; }
+extern "C" int b200_gemm_version(void) { return 101; }
 
 #ifdef B200_GEMM_PROFILE
 // Copies and clears the per-CTA wait counters (profiling builds only).
@@ -739,13 +749,13 @@ extern "C" int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int6
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
   if (p.bytes == 0)
-    return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, dev, stream);
+    return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiParams{}, dev, stream);
   if (p.bytes > kNoAllocScratchBytes) return B200_ERR_SCRATCH_LIMIT;
   uint8_t* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // Nothing in the scratch has to start at zero: the call writes every byte it
   // later reads (the re-pitched operand rows, and all of C's copy) first.
-  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiScale{}, p, scratch, dev,
+  return gemm_repacked(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiParams{}, p, scratch, dev,
                        stream);
 }
 
@@ -832,11 +842,108 @@ extern "C" int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M
                                                           row_b ? 1 : 0, cnorm);
   if (cudaGetLastError() != cudaSuccess) return B200_ERR_CUDA;
   if (cudaMemsetAsync(keys, 0xff, M * 8, stream) != cudaSuccess) return B200_ERR_CUDA;
-  GemmArgs g{X, Cent, nullptr, (int)M, (int)N, (int)K, ldx, ldcent, 0, EpiScale{}, dev.sm_count, stream};
+  GemmArgs g{X, Cent, nullptr, (int)M, (int)N, (int)K, ldx, ldcent, 0, EpiParams{}, dev.sm_count, stream};
   g.argmin.cnorm = cnorm;
   g.argmin.keys = keys;
   const int rc = row_b ? launch_skinny<5, 1, true, false, true>(g) : launch_skinny<5, 1, false, false, true>(g);
   if (rc) return rc;
   unpack_keys_kernel<<<(unsigned)((M + 255) / 256), 256, 0, stream>>>(keys, (int)M, out_idx, out_score);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Gathered output (multi-GPU): every rank computes its row shard of C and its
+// epilogue writes each finished block both to its own copy of the gathered C
+// and, with plain 16-byte stores over NVLink, to every peer's copy, so the
+// all-gather of C runs tile by tile under the GEMM instead of after it.  The
+// peers' buffers come from this library's IPC helpers (legacy CUDA IPC: one
+// cudaMalloc per buffer, no multicast object).  The kernels never wait on a
+// peer: completion is the caller's device-side barrier after the launch.
+// ---------------------------------------------------------------------------
+namespace b200 {
+
+// K == 0 in gathered mode: zero this shard's rows in the local and every peer
+// buffer (plain stores, like the epilogue's).
+__global__ void zero_rows_kernel(uint16_t* c, const __grid_constant__ EpiParams ep, int64_t rows, int64_t cols) {
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    for (int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; col < cols;
+         col += (int64_t)gridDim.x * blockDim.x) {
+      c[r * ep.ldc + col] = 0;
+      for (int p = 0; p < ep.n_peers; ++p) ep.peer[p][r * ep.ldc + col] = 0;
+    }
+  if (ep.n_peers > 0) __threadfence_system();
+}
+
+}  // namespace b200
+
+extern "C" int b200_ipc_handle_size(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int b200_ipc_alloc(int64_t bytes, void** ptr, void* handle) {
+  if (bytes <= 0 || !ptr || !handle) return B200_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return B200_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return B200_ERR_CUDA;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return B200_OK;
+}
+
+extern "C" int b200_ipc_free(void* ptr) {
+  if (!ptr) return B200_OK;
+  return cudaFree(ptr) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" int b200_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return B200_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return B200_ERR_CUDA;
+  *ptr = p;
+  return B200_OK;
+}
+
+extern "C" int b200_ipc_close(void* ptr) {
+  if (!ptr) return B200_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+extern "C" int b200_gemm_f16_gather(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                    int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* const* peer_c,
+                                    int n_peers, void* stream_ptr) {
+  using namespace b200;
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_c)) return B200_ERR_INVALID_ARGUMENT;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, lda, ldb, ldc, b_layout, A, B, &done)) return rc;
+  if (done) return B200_OK;
+  EpiParams ep;
+  ep.n_peers = n_peers;
+  ep.m = (int)M;
+  ep.n = (int)N;
+  ep.ldc = ldc;
+  for (int p = 0; p < n_peers; ++p) {
+    if (!peer_c[p]) return B200_ERR_INVALID_ARGUMENT;
+    if (!aligned16(peer_c[p])) return B200_ERR_MISALIGNED;
+    ep.peer[p] = static_cast<uint16_t*>(peer_c[p]);
+  }
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return rc;
+  if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (K == 0) {
+    const unsigned gx = (unsigned)std::min<int64_t>((N + 255) / 256, 64);
+    const unsigned gy = (unsigned)std::min<int64_t>(M, 65535);
+    zero_rows_kernel<<<dim3(gx, gy), 256, 0, stream>>>(static_cast<uint16_t*>(C), ep, M, N);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
+  // Operands must be TMA-addressable as they are: a re-pitched C would leave
+  // the peers' copies unwritten.
+  if (plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout, B200_A_ROW_MAJOR).bytes != 0) return B200_ERR_MISALIGNED;
+  return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, ep, dev, stream);
 }

@@ -106,30 +106,86 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 
 namespace b200 {
 
-// Epilogue scaling, the reference kernels' alpha / beta (tensorcore_gemm/
-// gemm.cu:1360-1364): C = fp16_rn(alpha * acc) when beta == 0, otherwise
-// C = fp16_rn(alpha * acc + beta * C_old), in fp32 with one rounding.
-struct EpiScale {
+constexpr int kMaxPeers = 7;
+
+// Epilogue parameters.
+//  * alpha / beta, the reference kernels' scaling (tensorcore_gemm/gemm.cu
+//    :1360-1364): C = fp16_rn(alpha * acc) when beta == 0, otherwise
+//    C = fp16_rn(alpha * acc + beta * C_old), in fp32 with one rounding.
+//  * m, n, ldc: C's extent and pitch (elements).
+//  * n_tma: C's columns [0, n_tma) go through the TMA tensor map (encoded
+//    n_tma wide).  A TMA store writes whole 16-byte pieces, so when n is not a
+//    multiple of 8 the map stops at n rounded down to 8 and the last partial
+//    piece of each row, columns [n_tma, n), is written by plain stores
+//    through `c` (and, with beta != 0, its old values read by plain loads).
+//  * peers (gathered-output mode): every finished C block is also written,
+//    with plain 16-byte stores, to `n_peers` other buffers of the same pitch
+//    -- the other GPUs' copies of the gathered C, mapped into this process
+//    by CUDA IPC, each pointer at this shard's first row.  Never a TMA or
+//    bulk access to peer memory.
+struct EpiParams {
   float alpha = 1.0f;
   float beta = 0.0f;
+  int m = 0;
+  int n = 0;
+  int n_tma = 0;
+  int n_peers = 0;
+  int64_t ldc = 0;
+  uint16_t* c = nullptr;
+  uint16_t* peer[kMaxPeers] = {};
 };
+
+// Copies the 16-byte pieces of the 32 x 64 fp16 block staged at `buf`
+// (128B-swizzled, row r at r * 128) whose columns lie in [c_lo, ep.n) to
+// element (x, y) of each of the `ndst` row-pitch-ldc buffers in `dst`.  Lane l
+// moves piece l % 8 of rows l / 8, l / 8 + 4, ...: one store instruction
+// writes four whole 128-byte row pieces.  A piece crossing ep.n is written
+// element by element.
+__device__ __forceinline__ void epi_plain_store(const uint8_t* buf, int lane, int x, int y, const EpiParams& ep,
+                                                int c_lo, uint16_t* const* dst, int ndst) {
+  const int seg = lane & 7;
+  const int col = x + seg * 8;
+  if (col >= ep.n || col + 8 <= c_lo) return;
+  const bool whole = col + 8 <= ep.n;
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    if (y + r >= ep.m) break;
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4));
+    const int64_t off = static_cast<int64_t>(y + r) * ep.ldc + col;
+#pragma unroll 1
+    for (int p = 0; p < ndst; ++p) {
+      uint16_t* d = dst[p] + off;
+      if (whole) {
+        *reinterpret_cast<uint4*>(d) = v;
+      } else {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 7; ++e)
+          if (e < ep.n - col) d[e] = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
+      }
+    }
+  }
+}
 
 // Writes one 32-row x 64-column block of C from the calling warp: lane l holds
 // row l's 64 fp32 values in lo (columns 0..31) and hi (32..63).  The block goes
 // through the warp's 128B-swizzled staging buffer (`NBUF` buffers, `sbuf`
-// rotates) and leaves with a TMA store at element (x, y) of C.  With beta != 0
-// the old C block is first brought into the same buffer by a TMA load that
-// completes on `cbar` (phase bit in `cphase`); the wait is bounded like every
-// other wait of the kernels.
+// rotates) and leaves with a TMA store at element (x, y) of C (plus plain
+// stores for a partial last piece and for the peers, see EpiParams).  With
+// beta != 0 the old C block is first brought into the same buffer by a TMA
+// load that completes on `cbar` (phase bit in `cphase`); the wait is bounded
+// like every other wait of the kernels.
 template <int NBUF>
 __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8_t* epi_buf, uint32_t epi_addr,
                                                 int& sbuf, int lane, const uint32_t (&lo)[32],
-                                                const uint32_t (&hi)[32], int x, int y, const EpiScale& sc,
+                                                const uint32_t (&hi)[32], int x, int y, const EpiParams& sc,
                                                 uint64_t* cbar, uint32_t& cphase) {
   if (lane == 0) bulk_wait_group_read<NBUF - 1>();
   __syncwarp();
   uint8_t* buf = epi_buf + sbuf * kEpiBufBytes;
   const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
+  const bool tma_part = x < sc.n_tma;       // some of the block's columns go through the map
   if (sc.alpha == 1.0f && sc.beta == 0.0f) {
     // Plain product (every call of the reference's launcher): pack the
     // accumulator bits directly; the skinny shapes are bound by this loop.
@@ -139,57 +195,75 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
       st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pack_half2_rn(v[0], v[1]), pack_half2_rn(v[2], v[3]),
                    pack_half2_rn(v[4], v[5]), pack_half2_rn(v[6], v[7]));
     }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tmap_c, buf, x, y);
-      bulk_commit_group();
-    }
-    sbuf = (sbuf + 1) % NBUF;
-    return;
-  }
-  bool have_old = false;
-  if (sc.beta != 0.0f) {
-    bool ok = true;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(cbar, kEpiBufBytes);
-      tma_load_2d(buf, tmap_c, cbar, x, y, policy_evict_first());
-      ok = mbar_wait(cbar, cphase, kDevTimeoutEpilogue);
-    }
-    cphase ^= 1u;
-    have_old = __shfl_sync(0xffffffffu, ok, 0);
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
-    const uint32_t addr = row_addr + ((j ^ (lane & 7)) << 4);
-    float f[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = sc.alpha * __uint_as_float(v[e]);
-    if (have_old) {
-      uint32_t o[4];
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-                   : "r"(addr));
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(&o[e]));
-        f[2 * e] = fmaf(sc.beta, old.x, f[2 * e]);
-        f[2 * e + 1] = fmaf(sc.beta, old.y, f[2 * e + 1]);
+  } else {
+    bool have_old = false;
+    if (sc.beta != 0.0f) {
+      bool ok = true;
+      if (lane == 0 && tma_part) {
+        mbar_arrive_expect_tx(cbar, kEpiBufBytes);
+        tma_load_2d(buf, tmap_c, cbar, x, y, policy_evict_first());
+        ok = mbar_wait(cbar, cphase, kDevTimeoutEpilogue);
       }
+      if (tma_part) cphase ^= 1u;
+      have_old = __shfl_sync(0xffffffffu, ok, 0);
     }
-    st_shared_v4(addr, pack_half2_rn(__float_as_uint(f[0]), __float_as_uint(f[1])),
-                 pack_half2_rn(__float_as_uint(f[2]), __float_as_uint(f[3])),
-                 pack_half2_rn(__float_as_uint(f[4]), __float_as_uint(f[5])),
-                 pack_half2_rn(__float_as_uint(f[6]), __float_as_uint(f[7])));
+    const int row = y + lane;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* v = (j < 4) ? (lo + 8 * j) : (hi + 8 * (j - 4));
+      const uint32_t addr = row_addr + ((j ^ (lane & 7)) << 4);
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = sc.alpha * __uint_as_float(v[e]);
+      if (have_old) {
+        const int col = x + 8 * j;
+        uint32_t o[4];
+        if (col + 8 <= sc.n_tma) {
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+                       : "r"(addr));
+        } else {
+          // Past the map: the old values of the partial piece come from C itself.
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[e] = 0;
+          if (row < sc.m) {
+            const uint16_t* src = sc.c + static_cast<int64_t>(row) * sc.ldc + col;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (col + e < sc.n) o[e >> 1] |= static_cast<uint32_t>(src[e]) << ((e & 1) * 16);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 old = __half22float2(*reinterpret_cast<const __half2*>(&o[e]));
+          f[2 * e] = fmaf(sc.beta, old.x, f[2 * e]);
+          f[2 * e + 1] = fmaf(sc.beta, old.y, f[2 * e + 1]);
+        }
+      }
+      st_shared_v4(addr, pack_half2_rn(__float_as_uint(f[0]), __float_as_uint(f[1])),
+                   pack_half2_rn(__float_as_uint(f[2]), __float_as_uint(f[3])),
+                   pack_half2_rn(__float_as_uint(f[4]), __float_as_uint(f[5])),
+                   pack_half2_rn(__float_as_uint(f[6]), __float_as_uint(f[7])));
+    }
   }
   fence_proxy_async_smem();
   __syncwarp();
-  if (lane == 0) {
+  if (lane == 0 && tma_part) {
     tma_store_2d(tmap_c, buf, x, y);
     bulk_commit_group();
   }
-  sbuf = (sbuf + 1) % NBUF;
+  if (sc.n_tma < sc.n && x + kEpiCols > sc.n_tma) epi_plain_store(buf, lane, x, y, sc, sc.n_tma, &sc.c, 1);
+  if (sc.n_peers > 0) epi_plain_store(buf, lane, x, y, sc, 0, sc.peer, sc.n_peers);
+  // The ring advances with the bulk groups: a block past the map committed
+  // none, so its buffer (only read synchronously) is reused by the next block;
+  // otherwise the wait above would count one group short.
+  if (tma_part) sbuf = (sbuf + 1) % NBUF;
+}
+
+// End of an epilogue warp in gathered-output mode: its peer stores are
+// performed system-wide before the kernel can complete.
+__device__ __forceinline__ void epi_peer_fence(const EpiParams& ep) {
+  if (ep.n_peers > 0) __threadfence_system();
 }
 
 }  // namespace b200

@@ -9,7 +9,7 @@ template <int BN, int STAGES, bool kBRowMajor, bool kAColMajor>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                             const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
-                            const EpiScale sc) {
+                            const __grid_constant__ EpiParams sc) {
   using Cfg = TileConfig<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            &c_bar[ew], c_phase);
       }
     }
+    epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();
   }
 

@@ -56,7 +56,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
-                                 const EpiScale sc) {
+                                 const __grid_constant__ EpiParams sc) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
   constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -300,6 +300,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
+    epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();
   }
 

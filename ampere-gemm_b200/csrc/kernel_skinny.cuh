@@ -40,7 +40,7 @@ template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kAr
 __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
     gemm_f16_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K,
-                           const EpiScale sc, const ArgminOut am = ArgminOut{}) {
+                           const __grid_constant__ EpiParams sc, const ArgminOut am = ArgminOut{}) {
   using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
   // The argmin epilogue is instruction-bound, so it runs on 8 warps (two per
   // TMEM lane quadrant, each on half of the columns); the store epilogue
@@ -282,6 +282,7 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
           atomicMin(am.keys + row, ((unsigned long long)float_to_ordered(best_d) << 32) | (unsigned)best_i);
       }
     }
+    epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();
   }
 

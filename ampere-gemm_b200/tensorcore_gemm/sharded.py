@@ -70,3 +70,114 @@ def all_gather_rows(C_shard: torch.Tensor, M: int, group=None, align: int = SHAR
     full = torch.empty((rows * world, N), dtype=C_shard.dtype, device=C_shard.device)
     dist.all_gather_into_tensor(full, padded, group=group)
     return torch.cat([full[r * rows: r * rows + (b - a)] for r, (a, b) in enumerate(bounds)], dim=0)
+
+
+def peer_shard_ptrs(peer_bases: list[int], row0: int, ldc: int, elem_bytes: int = 2) -> list[int]:
+    """Addresses of this shard's first row in every peer's copy of the gathered C."""
+    return [int(b) + int(row0) * int(ldc) * elem_bytes for b in peer_bases]
+
+
+class _DeviceBuffer:
+    """A raw device allocation exposed to torch (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, rows: int, cols: int):
+        self.__cuda_array_interface__ = {"shape": (rows, cols), "typestr": "<f2", "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class GatheredOutput:
+    """The full M x N C on every rank, filled by the fused gathered-output GEMM.
+
+    Every rank allocates its copy of C as one IPC-shareable buffer (legacy
+    CUDA IPC, no multicast object) and maps every peer's copy.  `gemm` then
+    runs this rank's row shard with b200_gemm_f16_gather: each finished C
+    block goes to the local copy with a TMA store and to every peer's copy
+    with plain 16-byte stores over NVLink, so the all-gather rides under the
+    GEMM.  A one-element all-reduce on the current stream afterwards is the
+    device-side barrier after which every rank's copy holds all rows.
+    Collective: every rank of `group` constructs it, calls `gemm` and
+    `close` in the same order.
+    """
+
+    def __init__(self, M: int, N: int, group=None, device: torch.device | None = None,
+                 align: int = SHARD_ALIGN_ROWS):
+        import torch.distributed as dist
+
+        from . import _native
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world - 1 > 7:
+            raise ValueError("the gathered output supports at most 8 ranks")
+        self.M, self.N, self.align = int(M), int(N), align
+        self.ldc = max(8, -(-self.N // 8) * 8)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            self._ptr, handle = _native.ipc_alloc(max(1, self.M) * self.ldc * 2)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle, group=group)
+            self._peers = [_native.ipc_open(h) for r, h in enumerate(handles) if r != self.rank]
+            self._buf = _DeviceBuffer(self._ptr, max(1, self.M), self.ldc)
+            self._full = torch.as_tensor(self._buf, device=self.device)
+            self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._closed = False
+
+    @property
+    def full(self) -> torch.Tensor:
+        """This rank's copy of the gathered C (M x N view of the M x ldc buffer)."""
+        return self._full[: self.M, : self.N]
+
+    def bounds(self) -> tuple[int, int]:
+        return row_shard_bounds(self.M, self.world, self.rank, self.align)
+
+    def gemm(self, A_shard: torch.Tensor, B: torch.Tensor, b_col_major: bool = False) -> torch.Tensor:
+        """Fill `full` with [A_0; A_1; ...] @ B, A_r being rank r's rows (B as K x N, or N x K if b_col_major)."""
+        import torch.distributed as dist
+
+        from . import _native
+        from .gemm import _check_operands, _current_stream
+        from .kmeans import _pitched
+
+        if self._closed:
+            raise RuntimeError("GatheredOutput is closed")
+        lo, hi = self.bounds()
+        Bk = B.t() if b_col_major else B
+        _check_operands(A_shard, Bk)
+        if A_shard.shape[0] != hi - lo:
+            raise RuntimeError(f"rank {self.rank} shard has {A_shard.shape[0]} rows, expected {hi - lo}")
+        if Bk.shape[1] != self.N:
+            raise RuntimeError(f"B has {Bk.shape[1]} columns, the gathered output {self.N}")
+        if not b_col_major and B.stride(0) == 1 and B.stride(1) >= max(1, B.shape[0]) and B.size(0) > 1:
+            B, b_col_major = B.t(), True   # transposed view of an N x K buffer
+        A = _pitched(A_shard)
+        B = _pitched(B)
+        layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
+        K = A.shape[1]
+        c_ptr = self._ptr + lo * self.ldc * 2
+        with torch.cuda.device(self.device):
+            code = _native.gemm_gather_raw(A.data_ptr(), B.data_ptr(), c_ptr, hi - lo, self.N, K,
+                                           A.stride(0), B.stride(0),
+                                           self.ldc, layout, peer_shard_ptrs(self._peers, lo, self.ldc),
+                                           _current_stream(self.device.index))
+            _native.check(code, "b200_gemm_f16_gather")
+            dist.all_reduce(self._flag, group=self.group)
+        return self.full
+
+    def close(self) -> None:
+        """Unmap the peers' copies, then free this rank's (collective)."""
+        import torch.distributed as dist
+
+        from . import _native
+
+        if self._closed:
+            return
+        self._closed = True
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            for p in self._peers:
+                _native.ipc_close(p)
+            dist.barrier(group=self.group)
+            self._full = None
+            _native.ipc_free(self._ptr)

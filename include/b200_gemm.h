@@ -142,6 +142,40 @@ B200_API int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M, 
                                     int64_t ldcent, int cent_layout, void* workspace, int64_t workspace_bytes,
                                     int32_t* out_idx, float* out_score, void* stream);
 
+/*
+ * Gathered output: C = A * B for this rank's row shard, where every finished
+ * C block is written both to C (this GPU's copy of the gathered matrix, at
+ * the shard's first row) and to each of the `n_peers` (<= 7) buffers in
+ * peer_c -- the other GPUs' copies, mapped into this process by
+ * b200_ipc_open, each pointer at the same shard offset, all with pitch ldc.
+ * The all-gather of C so runs tile by tile under the GEMM, as plain 16-byte
+ * stores over NVLink.  The reference has no multi-GPU code; this is the
+ * fused form of its optional gathered-output step (a GEMM followed by an
+ * all-gather of the C shards).  Operands must be TMA-compatible as given
+ * (B200_ERR_MISALIGNED otherwise).  The kernel never waits on a peer: when
+ * the call's work on `stream` is done, this rank's stores are visible to
+ * every peer; the caller synchronises the ranks (a device-side barrier such
+ * as a one-element NCCL all-reduce on the same stream) before any rank reads
+ * the rows that others wrote.
+ */
+B200_API int b200_gemm_f16_gather(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                  int64_t lda, int64_t ldb, int64_t ldc, int b_layout, void* const* peer_c,
+                                  int n_peers, void* stream);
+
+/*
+ * Device buffers shareable across processes (legacy CUDA IPC), for the
+ * gathered output above.  b200_ipc_alloc allocates `bytes` on the current
+ * device and writes its b200_ipc_handle_size()-byte handle; another process
+ * maps it with b200_ipc_open and unmaps it with b200_ipc_close; the owner
+ * frees it with b200_ipc_free after every peer has closed it.  No multicast
+ * object is created.  No counterpart in the reference.
+ */
+B200_API int b200_ipc_handle_size(void);
+B200_API int b200_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+B200_API int b200_ipc_free(void* ptr);
+B200_API int b200_ipc_open(const void* handle, void** ptr);
+B200_API int b200_ipc_close(void* ptr);
+
 /* Human-readable text of a return code (static storage). Counterpart of the
  * TORCH_CHECK messages of the reference launcher (gemm.py:33-47, 150-152). */
 B200_API const char* b200_gemm_strerror(int code);

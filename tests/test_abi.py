@@ -97,3 +97,24 @@ def test_workspace_size_plan(native_lib):
     assert ws(A + 2, B, C, 4, 8, 8, 8, 8, 8, 0) == 256                  # misaligned base only
     assert ws(A, B, C, 0, 8, 8, 8, 8, 8, 0) == 0                        # empty output
     assert ws(A, B, C, 4, 8, 8, 4, 8, 8, 0) == -_native.B200_ERR_INVALID_ARGUMENT   # lda < K
+
+
+def test_gather_argument_validation_without_gpu(native_lib):
+    """Checks of b200_gemm_f16_gather that come before any CUDA call."""
+    from tensorcore_gemm import _native
+
+    buf = ctypes.create_string_buffer(4096)
+    base = (ctypes.addressof(buf) + 15) & ~15
+    assert _native.gemm_gather_raw(base, base, base, 8, 8, 8, 8, 8, 8, 0, [base] * 8, 0) == \
+        _native.B200_ERR_INVALID_ARGUMENT                                   # more than 7 peers
+    assert _native.gemm_gather_raw(base, base, base, 8, 8, 8, 8, 8, 8, 0, [0], 0) == \
+        _native.B200_ERR_INVALID_ARGUMENT                                   # null peer
+    assert _native.gemm_gather_raw(base, base, base, 8, 8, 8, 8, 8, 8, 0, [base + 8], 0) == \
+        _native.B200_ERR_MISALIGNED                                         # peer not 16-byte aligned
+    assert _native.gemm_gather_raw(base, base, base, 0, 8, 8, 8, 8, 8, 0, [base], 0) == _native.B200_OK
+    lib = _native.load()
+    assert lib.b200_ipc_handle_size() == 64
+    ptr = ctypes.c_void_p()
+    assert lib.b200_ipc_alloc(0, ctypes.byref(ptr), buf) == _native.B200_ERR_INVALID_ARGUMENT
+    assert lib.b200_ipc_open(None, ctypes.byref(ptr)) == _native.B200_ERR_INVALID_ARGUMENT
+    assert lib.b200_ipc_close(None) == _native.B200_OK and lib.b200_ipc_free(None) == _native.B200_OK

@@ -1,4 +1,5 @@
-"""GPU, 2+ devices: row-sharded GEMM on each rank plus the NCCL all-gather of C.
+"""GPU, 2+ devices: row-sharded GEMM on each rank plus the NCCL all-gather of
+C, and the fused gathered-output GEMM (peer stores from the epilogue).
 
 Skipped when fewer than two GPUs are visible.  Each rank is its own process
 (one process per GPU); no kernel waits on another GPU.
@@ -68,3 +69,62 @@ def test_two_rank_sharded_gemm_and_all_gather(native_lib):
     res = [q.get(timeout=30) for _ in procs]
     assert all(p.exitcode == 0 for p in procs)
     assert all(ok for _, ok, _, _ in res), res
+
+
+def _gather_worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for p in (str(repo), str(repo / "ampere-gemm_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensorcore_gemm import _native, sharded
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    out = None
+    try:
+        results = []
+        for (M, N, K, colb) in [(1000, 264, 512, False), (3000, 1001, 256, True), (2048, 2048, 2048, False)]:
+            A, B = oracle.make_inputs(M, N, K, dist="normal", seed_a=41 + M, seed_b=42 + N, std=0.02)
+            out = sharded.GatheredOutput(M, N, device=dev)
+            lo, hi = out.bounds()
+            Bd = B.to(dev)
+            full = out.gemm(A[lo:hi].to(dev), Bd.t().contiguous() if colb else Bd, b_col_major=colb)
+            torch.cuda.synchronize()
+            ref = A.float() @ B.float()
+            err = (full.float().cpu() - ref).abs().max().item()
+            bound = 2e-3 * K ** 0.5 * ref.pow(2).mean().sqrt().item()
+            # Rows written by the peers must equal what the plain path computes there.
+            results.append(err <= bound)
+            out.close()
+            out = None
+        q.put((rank, all(results) and _native.last_device_error() == 0, results))
+    finally:
+        if out is not None:
+            out.close()
+        dist.destroy_process_group()
+
+
+def test_two_rank_gathered_output(native_lib):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    res = [q.get(timeout=30) for _ in procs]
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(ok for _, ok, _ in res), res

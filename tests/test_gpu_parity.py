@@ -151,6 +151,35 @@ def test_output_guard_bands_untouched(cuda_device, variant):
     assert (buf[mask] == 7.0).all(), "kernel wrote outside the output view"
 
 
+@pytest.mark.parametrize("N,alpha,beta", [(1001, 1.0, 0.0), (1001, 0.5, -1.25), (5, 1.0, 0.0), (5, 2.0, 0.5),
+                                           (263, 1.0, 0.0)])
+def test_output_guard_columns_ragged_n(cuda_device, variant, N, alpha, beta):
+    """N not a multiple of 8 inside a wider buffer: the columns right after the
+    view (inside the same 16-byte piece) keep their values; alpha / beta are
+    applied to the ragged last piece as to every other column."""
+    M, K = 300, 192
+    A, B = _inputs(M, N, K, cuda_device)
+    ld = 1024
+    buf = torch.full((M + 16, ld), 7.0, dtype=torch.float16, device=cuda_device)
+    off = 8
+    view = buf[8:8 + M, off:off + N]
+    old = (torch.randn((M, N), device=cuda_device) * 0.5).half()
+    view.copy_(old)
+    from tensorcore_gemm.kmeans import _pitched
+
+    Bp = _pitched(B)                            # row pitch a multiple of 8: no workspace needed
+    code = _native.gemm_ex_raw(A.data_ptr(), Bp.data_ptr(), view.data_ptr(), M, N, K, K, Bp.stride(0), ld,
+                               _native.B200_A_ROW_MAJOR, _native.B200_B_ROW_MAJOR, alpha, beta,
+                               0, 0, torch.cuda.current_stream().cuda_stream)
+    assert code == 0
+    torch.cuda.synchronize()
+    ref = alpha * fp32_ref(A, B) + beta * old.float()
+    assert_parity(view, ref, K)
+    mask = torch.ones_like(buf, dtype=torch.bool)
+    mask[8:8 + M, off:off + N] = False
+    assert (buf[mask] == 7.0).all(), "kernel wrote outside the output view"
+
+
 def test_strided_views_without_copies(cuda_device, variant):
     """Row-strided A, and B given as a transposed view, run in place."""
     big = torch.randn((300, 512), device=cuda_device).half()

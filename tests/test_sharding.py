@@ -64,3 +64,12 @@ def test_all_gather_two_gloo_ranks(M):
     results = dict(q.get(timeout=10) for _ in procs)
     assert all(p.exitcode == 0 for p in procs)
     assert results == {0: True, 1: True}
+
+
+def test_peer_shard_pointers():
+    """Each peer pointer is that peer's buffer base plus the shard's first row (fp16, pitch ldc)."""
+    bases = [0x7f0000000000, 0x7f1000000000, 0x7f2000000000]
+    lo, _ = sharded.row_shard_bounds(65536, 8, 5)
+    ptrs = sharded.peer_shard_ptrs(bases, lo, 8192)
+    assert ptrs == [b + lo * 8192 * 2 for b in bases]
+    assert all(p % 16 == 0 for p in ptrs)
