@@ -373,7 +373,79 @@ def side_measurements(torch, tg, dev, peaks) -> dict:
         res[name + "_TFLOPs"] = round(fl / (ms * 1e-3) / 1e12, 1)
     res["rowB_frac_of_measured_bf16_burst"] = round(res["rowB_TFLOPs"] / peaks["bf16_tflops"], 4)
     out["square_8192"] = res
+    del ops, opsc, Cbuf
+    out["kmeans_assign_262144x1024x256"] = kmeans_measurement(torch, dev, g)
     return out
+
+
+def kmeans_measurement(torch, dev, g) -> dict:
+    """Fused K-means assignment (argmin in the skinny GEMM's epilogue) against
+    torch.mm + argmin on the same points; two point sets (> L2 together)."""
+    from tensorcore_gemm import kmeans
+
+    M, N, K = 262144, 1024, 256
+    pts = [torch.randn((M, K), generator=g, device=dev, dtype=torch.float16) for _ in range(2)]
+    cent = torch.randn((N, K), generator=g, device=dev, dtype=torch.float16)
+    fused = lambda i: kmeans.assign(pts[i % 2], cent)
+    cn = cent.float().pow(2).sum(1)
+    plain = lambda i: torch.argmin(cn[None, :] - 2 * torch.mm(pts[i % 2], cent.t()).float(), 1)
+    agree = bool((fused(0).long() == plain(0)).float().mean().item() > 0.999)
+    for f in (fused, plain):
+        for i in range(4):
+            f(i)
+    ms_f = _time_launches(torch, fused, 40)
+    ms_p = _time_launches(torch, plain, 10)
+    moved = 2 * (M * K + N * K) + 4 * M
+    return {"fused_us": round(ms_f * 1e3, 1), "torch_mm_argmin_us": round(ms_p * 1e3, 1),
+            "speedup": round(ms_p / ms_f, 2), "fused_GBps": round(moved / (ms_f * 1e-3) / 1e9, 1),
+            "algorithmic_bytes": moved, "indices_agree_with_torch": agree,
+            "timing": "CUDA events over back-to-back calls through kmeans.assign (norms, argmin GEMM, unpack)"}
+
+
+def gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank, barrier, max_over_ranks,
+                                gemm_ms: float, steps: int = 5) -> dict:
+    """Full C on every rank: GEMM then NCCL all-gather, against the fused
+    gathered-output GEMM (epilogue peer stores).  Device time, max over ranks."""
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        barrier()
+        ev0.record(stream)
+        for _ in range(steps):
+            fn()
+        ev1.record(stream)
+        ev1.synchronize()
+        barrier()
+        return max_over_ranks(ev0.elapsed_time(ev1)) / steps
+
+    full_nccl = torch.empty((C.shape[0] * world, C.shape[1]), dtype=C.dtype, device=dev)
+
+    def separate():
+        sharded.sharded_gemm(A, B, out=C)
+        dist.all_gather_into_tensor(full_nccl, C)
+
+    ms_sep = timed(separate)
+    out = sharded.GatheredOutput(M_TOTAL, N_DIM, device=dev)
+    try:
+        ms_fused = timed(lambda: out.gemm(A, B))
+        same = torch.equal(out.full, full_nccl[:M_TOTAL])
+        flag = torch.tensor([0.0 if same else 1.0], device=dev)
+        dist.all_reduce(flag)
+        match = flag.item() == 0.0
+    finally:
+        out.close()
+    del full_nccl
+    gathered_bytes = 2 * M_TOTAL * N_DIM
+    return {"what": "C (65536 x 8192 fp16) gathered on every rank",
+            "gemm_only_ms": round(gemm_ms, 4),
+            "gemm_then_nccl_all_gather_ms": round(ms_sep, 4),
+            "fused_peer_store_ms": round(ms_fused, 4),
+            "fused_speedup": round(ms_sep / ms_fused, 3),
+            "nvlink_bytes_out_per_gpu": int(gathered_bytes * (world - 1) // world),
+            "bitwise_equal_to_nccl_path": bool(match), "steps": steps}
 
 
 def run_b200(args) -> int:
@@ -469,6 +541,11 @@ def run_b200(args) -> int:
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
     e2e_value = 2.0 * M_TOTAL * N_DIM * K_DIM * e2e_steps / (e2e_ms * 1e-3) / 1e12
 
+    gathered = None
+    if world > 1 and not args.no_extras:
+        gathered = gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank, barrier,
+                                               max_over_ranks, ms_max / args.steps)
+
     extras = None
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:
@@ -503,6 +580,8 @@ def run_b200(args) -> int:
             line["cpu_baseline"] = cpu
         if extras is not None:
             line["extras"] = extras
+        if gathered is not None:
+            line["gathered_output"] = gathered
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
