@@ -29,6 +29,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "gemm_common.cuh"
 #include "kernel_cta1.cuh"
@@ -177,6 +178,36 @@ int ensure_smem_attr(Kern kern, int smem_bytes, std::atomic<uint8_t>* done) {
   return B200_OK;
 }
 
+// GEMM kernels go out with programmatic stream serialisation (PDL): a kernel
+// may be scheduled while the previous one on the stream drains, runs its
+// setup (barriers, TMEM, tensor-map prefetch), and waits in griddep_wait()
+// before its first global access.  B200_GEMM_PDL=0 turns it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B200_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_gemm(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                        Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+
 // One GEMM call as the launchers see it (operands already TMA-compatible).
 struct GemmArgs {
   const void* A;
@@ -228,8 +259,9 @@ int launch_tcgen05(const GemmArgs& g, int group_m) {
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = (int)std::min<long long>(tiles, sm_count);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m, g.scale);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, ta, tb, tc, M, N, K,
+                                     group_m, g.scale);
+  return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 // Largest number of 2-CTA clusters of `kern` that can be resident at once
@@ -289,8 +321,9 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   }
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
-  kern<<<2 * grid_pairs, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, group_m, g.scale);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  const cudaError_t le = launch_gemm(kern, dim3(2 * grid_pairs), dim3(kThreads), Cfg::kSmemBytes, stream, ta, tb, tc,
+                                     M, N, K, group_m, g.scale);
+  return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 // Skinny (K <= 256) B-stationary kernel.  The grid is the largest multiple of
@@ -328,8 +361,9 @@ int launch_skinny(const GemmArgs& g) {
   const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
   const int slots = (sm_count / num_nb) * num_nb;
   const int grid = (int)std::min<long long>(tiles, slots);
-  kern<<<grid, kArgmin ? 320 : kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, M, N, K, g.scale, g.argmin);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3(kArgmin ? 320 : kThreads), Cfg::kSmemBytes, stream, ta, tb,
+                                     tc, M, N, K, g.scale, g.argmin);
+  return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 // Kernel choice for K > 256.  Each persistent variant runs its tiles in waves

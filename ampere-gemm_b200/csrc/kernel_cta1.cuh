@@ -60,6 +60,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_base_slot;
+  // Setup above overlaps the previous kernel on the stream; nothing below
+  // touches global memory before that kernel's results are visible.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer (one lane) ----------------

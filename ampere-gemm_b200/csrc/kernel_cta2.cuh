@@ -110,6 +110,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_base_slot;
+  // Setup above overlaps the previous kernel on the stream; nothing below
+  // touches global memory before that kernel's results are visible.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer (one lane per CTA) ----------------

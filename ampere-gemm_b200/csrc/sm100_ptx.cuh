@@ -358,4 +358,14 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// Programmatic dependent launch (PTX griddepcontrol, sm_90+).  `wait` blocks
+// until every grid this one depends on has completed and its memory is
+// visible (a no-op when the launch carried no programmatic dependency);
+// `launch_dependents` lets the next grid on the stream be scheduled before
+// this one ends.  Both are hardware operations, not spins of this code.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace b200
