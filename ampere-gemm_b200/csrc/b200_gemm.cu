@@ -330,9 +330,9 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
 // the number of 256-column N slices that fits the SMs, so every CTA keeps one
 // slice of B resident.  Returns B200_ERR_INVALID_ARGUMENT when the shape does
 // not qualify (caller falls back to another variant).
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false>
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false, int EPI_W = kEpiWarps>
 int launch_skinny(const GemmArgs& g) {
-  using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
+  using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS, EPI_W>;
   const void *A = g.A, *B = g.B;
   void* C = g.C;
   const int M = g.M, N = g.N, K = g.K;
@@ -355,13 +355,13 @@ int launch_skinny(const GemmArgs& g) {
   else
     rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor, kArgmin>;
+  auto kern = gemm_f16_skinny_kernel<A_STAGES, EPI_BUFS, kBRowMajor, kAColMajor, kArgmin, EPI_W>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
   const int slots = (sm_count / num_nb) * num_nb;
   const int grid = (int)std::min<long long>(tiles, slots);
-  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3(kArgmin ? 320 : kThreads), Cfg::kSmemBytes, stream, ta, tb,
+  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3((kArgmin || EPI_W == 8) ? 320 : kThreads), Cfg::kSmemBytes, stream, ta, tb,
                                      tc, M, N, K, g.scale, g.argmin);
   return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
@@ -491,6 +491,9 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   if (variant == B200_VARIANT_AUTO) variant = pick_tensor_variant(m, n, k, dev.sm_count);
   if (variant == B200_VARIANT_SKINNY) {
     const int rc = with_layouts(row_b, col_a, [&](auto rb, auto ca) {
+      // Measured: 5 A stages with 4 epilogue warps beat 4 stages with 8 warps
+      // (the A stream, not the epilogue, then sets the pace) and 4 stages
+      // with two staging buffers per warp.
       return launch_skinny<5, 1, decltype(rb)::value, decltype(ca)::value>(g);
     });
     if (rc != B200_ERR_INVALID_ARGUMENT) return rc;

@@ -22,30 +22,32 @@
 
 namespace b200 {
 
-template <int A_STAGES, int EPI_BUFS>
+template <int A_STAGES, int EPI_BUFS, int EPI_W = kEpiWarps>
 struct SkinnyConfig {
   static constexpr int kBN = 256;
   static constexpr int kMaxKBlocks = 4;                     // K <= 256
   static constexpr int kABytes = kBM * kBK * 2;             // 16 KB per A stage
   static constexpr int kBBlockBytes = kBN * kBK * 2;        // 32 KB per 64-deep K block of B
   static constexpr int kBBytes = kMaxKBlocks * kBBlockBytes;
-  static constexpr int kEpiBytes = kEpiWarps * EPI_BUFS * kEpiBufBytes;
+  static constexpr int kEpiBytes = EPI_W * EPI_BUFS * kEpiBufBytes;
   static constexpr int kTmemCols = 2 * kBN;
   static constexpr int kNormBytes = kBN * 4;                // argmin mode: the CTA's slice of ||c||^2
   static constexpr int kSmemBytes = kBBytes + A_STAGES * kABytes + kEpiBytes + kNormBytes + 256 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
-template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false>
-__global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
+template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false, int EPI_W = kEpiWarps>
+__global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
     gemm_f16_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K,
                            const __grid_constant__ EpiParams sc, const ArgminOut am = ArgminOut{}) {
-  using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS>;
-  // The argmin epilogue is instruction-bound, so it runs on 8 warps (two per
-  // TMEM lane quadrant, each on half of the columns); the store epilogue
-  // keeps 4 (its staging buffers would not fit twice).
-  constexpr int kEpiW = kArgmin ? 8 : kEpiWarps;
+  using Cfg = SkinnyConfig<A_STAGES, EPI_BUFS, EPI_W>;
+  // The epilogue sets the pace of this kernel (per tile it drains 128 x 256
+  // fp32 while the MMAs take ~2k cycles), so it may run on 8 warps: two per
+  // TMEM lane quadrant, each on half of the columns.  The argmin epilogue
+  // always does.
+  constexpr int kEpiW = kArgmin ? 8 : EPI_W;
+  static_assert(EPI_W == 4 || EPI_W == 8, "4 or 8 epilogue warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_b = smem;                                   // resident B slice
@@ -59,8 +61,8 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
   uint64_t* tmem_empty = bars + 2 * A_STAGES + 2;           // [2]
   uint64_t* b_full = bars + 2 * A_STAGES + 4;               // [4] B slice, one per 64-deep K block
   uint64_t* mma_drain = bars + 2 * A_STAGES + 8;            // [1] abort path only
-  uint64_t* c_bar = bars + 2 * A_STAGES + 9;                // [4] old-C loads of the epilogue warps (beta != 0)
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * A_STAGES + 13);
+  uint64_t* c_bar = bars + 2 * A_STAGES + 9;                // [8] old-C loads of the epilogue warps (beta != 0)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * A_STAGES + 17);
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
     }
     for (int kb = 0; kb < Cfg::kMaxKBlocks; ++kb) mbar_init(&b_full[kb], 1);
     mbar_init(mma_drain, 1);
-    for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
+    for (int e = 0; e < kEpiW; ++e) mbar_init(&c_bar[e], 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
+    // ---------------- epilogue warps 2 .. 1 + kEpiW ----------------
     const int quad = warp & 3;
     const int ew = warp - 2;
     constexpr int kChunksPerWarp = (Cfg::kBN / kEpiCols) * kEpiWarps / kEpiW;
@@ -234,16 +236,23 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after_sync();
+#ifdef B200_GEMM_PROFILE
+      const long long prof_e0 = clock64();
+#endif
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * Cfg::kBN;
       float best_d = __int_as_float(0x7f800000);  // +inf
       int best_i = 0x7fffffff;
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
         uint32_t lo[32], hi[32];
+#ifdef B200_GEMM_PROFILE
+        const long long prof_l0 = clock64();
+#endif
         tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
         tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
         tmem_ld_wait_regs(lo);
         tmem_ld_wait_regs(hi);
+        B200_PROF_ADD(6, clock64() - prof_l0);
         if (c == c_end - 1) {
           tc_fence_before_sync();
           __syncwarp();
@@ -285,6 +294,8 @@ __global__ void __launch_bounds__(kArgmin ? 320 : kThreads, 1)
         if (row < M && best_i != 0x7fffffff)
           atomicMin(am.keys + row, ((unsigned long long)float_to_ordered(best_d) << 32) | (unsigned)best_i);
       }
+      B200_PROF_ADD(5, clock64() - prof_e0);
+      B200_PROF_ADD(7, 1);
     }
     epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();

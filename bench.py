@@ -318,6 +318,22 @@ def read_traffic_per_launch(tag: str):
     return None
 
 
+def hbm_direction_peaks(torch, dev) -> dict:
+    """Read-only and write-only HBM bandwidth of plain torch kernels (sum and
+    fill_ over four rotating 128 MiB buffers, > L2 together, CUDA-graph
+    replay): the denominators for traffic that is mostly writes."""
+    n = 64 * 1024 * 1024
+    src = [torch.randn(n, device=dev).half() for _ in range(4)]
+    dst = [torch.empty(n, dtype=torch.float16, device=dev) for _ in range(4)]
+    ms_r = _time_graph(torch, lambda i: src[i % 4].sum(dtype=torch.float32), 40)
+    ms_w = _time_graph(torch, lambda i: dst[i % 4].fill_(1.0), 40)
+    out = {"read_only_GBps": round(2 * n / (ms_r * 1e-3) / 1e9, 1),
+           "write_only_GBps": round(2 * n / (ms_w * 1e-3) / 1e9, 1),
+           "how": "torch.sum (read) and Tensor.fill_ (write) over 4 rotating 128 MiB fp16 buffers, graph replay"}
+    del src, dst
+    return out
+
+
 def side_measurements(torch, tg, dev, peaks) -> dict:
     """N=1 only: skinny K=256 HBM bandwidth (cold L2), 8192^3 both layouts, torch.mm."""
     out = {}
@@ -343,6 +359,9 @@ def side_measurements(torch, tg, dev, peaks) -> dict:
     ms_col = _time_graph(torch, col, iters)
     ms_mm = _time_graph(torch, mm, iters)
     gbs = lambda ms: set_bytes / (ms * 1e-3) / 1e9
+    dirs = hbm_direction_peaks(torch, dev)
+    read_b, write_b = 2 * (M * K + K * N), 2 * M * N
+    bound_us = (read_b / dirs["read_only_GBps"] + write_b / dirs["write_only_GBps"]) / 1e3
     out["skinny_32768x1024x256"] = {
         "cold_l2": f"{nsets} rotating operand sets of {set_bytes / 1e6:.1f} MB (> 2x L2)",
         "timing": "CUDA-graph replay of back-to-back launches (device time, no host gaps)",
@@ -353,6 +372,11 @@ def side_measurements(torch, tg, dev, peaks) -> dict:
         "roofline": {"bound": "hbm", "achieved": round(gbs(ms_row), 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gbs(ms_row) / peaks["hbm_gbs"], 4),
                      "traffic": read_traffic_per_launch("skinny_32768x1024x256")},
+        "direction_roofline": {"what": "reads at the read-only rate plus writes at the write-only rate",
+                               "read_bytes": read_b, "write_bytes": write_b, **dirs,
+                               "bound_us": round(bound_us, 2),
+                               "rowB_frac": round(bound_us / (ms_row * 1e3), 4),
+                               "colb_frac": round(bound_us / (ms_col * 1e3), 4)},
     }
     del sets, bcol
     # --- 8192^3, uniform inputs, both layouts; two operand sets (> L2 together)
