@@ -287,6 +287,99 @@ int max_active_pairs(Kern kern, int smem_bytes, int sm_count) {
   return n;
 }
 
+// ---- split of the last wave along K (pair kernel, MSUB = 1) ----
+// Cost model in SM cycles: a 256 x 256 pair tile spends 1024 cycles per
+// 128-deep K stage.  A split tail costs about 12.4k cycles for writing the
+// unit's 128 KB part and arriving, plus 3k per K range for the last unit's
+// read-back and sum (profile build, 1.9 GHz: 3.7-4.0 us per part write, 5.6 us
+// fixup at S = 2, 7.1-7.4 us at S = 3).  So only deep K pays: at K <= 4096 the
+// last wave stays whole.
+constexpr double kPairStageCycles = 1024.0;
+constexpr double kSplitFixedCycles = 12400.0;
+constexpr double kSplitPartCycles = 3000.0;
+
+// K ranges per tail tile that minimise the last wave's time (1 = no split).
+int choose_split(int num_kb, long long smax) {
+  int best = 1;
+  double best_cost = num_kb * kPairStageCycles;
+  for (int S = 2; S <= smax && S <= 16 && 2 * S <= num_kb; ++S) {
+    const double c = num_kb * kPairStageCycles / S + kSplitFixedCycles + kSplitPartCycles * S;
+    if (c < best_cost * 0.97) {
+      best_cost = c;
+      best = S;
+    }
+  }
+  return best;
+}
+
+// Last wave's time as a fraction of a whole tile's, with the split the
+// launcher would choose.
+double pair_tail_fraction(int num_kb, long long tiles, int slots) {
+  const long long r = tiles % slots;
+  if (r == 0) return 1.0;
+  if (tiles < slots) return 1.0;  // a single partial wave is never split
+  const int S = choose_split(num_kb, slots / r);
+  if (S == 1) return 1.0;
+  return (num_kb * kPairStageCycles / S + kSplitFixedCycles + kSplitPartCycles * S) / (num_kb * kPairStageCycles);
+}
+
+bool split_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B200_GEMM_SPLIT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// One workspace per (device, stream): launches on one stream are ordered, so
+// they can share it; other streams get their own.  Allocated on first use
+// (never during a stream capture: that launch then runs unsplit).
+struct SplitWorkspace {
+  int dev;
+  cudaStream_t stream;
+  float* parts;
+  uint32_t* counters;
+  int max_parts;
+  uint32_t seq;
+};
+
+std::mutex g_split_mu;
+SplitWorkspace g_split_ws[64];
+int g_split_n = 0;
+
+bool split_workspace(cudaStream_t stream, int sm_count, SplitTail& st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_split_mu);
+  SplitWorkspace* w = nullptr;
+  for (int i = 0; i < g_split_n; ++i)
+    if (g_split_ws[i].dev == dev && g_split_ws[i].stream == stream) w = &g_split_ws[i];
+  if (!w) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+    if (g_split_n == 64) return false;
+    const int max_parts = sm_count;  // R * S <= pairs, two CTAs each
+    const size_t part_bytes = (size_t)max_parts * kPartFloats * sizeof(float);
+    void* mem = nullptr;
+    if (cudaMalloc(&mem, part_bytes + (size_t)max_parts * sizeof(uint32_t)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(mem) + part_bytes);
+    if (cudaMemsetAsync(ctr, 0, (size_t)max_parts * sizeof(uint32_t), stream) != cudaSuccess) {
+      cudaFree(mem);
+      return false;
+    }
+    w = &g_split_ws[g_split_n++];
+    *w = SplitWorkspace{dev, stream, static_cast<float*>(mem), ctr, max_parts, 0};
+  }
+  w->seq = (w->seq % 0xffffffu) + 1u;  // 1 .. 2^24 - 1
+  st.ws = w->parts;
+  st.counters = w->counters;
+  st.seq = w->seq;
+  return true;  // R * S <= pairs <= sm_count / 2, so the parts always fit
+}
+
 template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
 int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
@@ -321,8 +414,23 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   }
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
+  SplitTail st;
+  if (MSUB == 1 && split_enabled() && tiles > grid_pairs && tiles % grid_pairs != 0) {
+    const int num_kb = (K + Cfg::kStageK - 1) / Cfg::kStageK;
+    const long long r = tiles % grid_pairs;
+    const int S = choose_split(num_kb, grid_pairs / r);
+    if (S >= 2) {
+      SplitTail s2;
+      s2.dp_tiles = (int)(tiles - r);
+      s2.S = S;
+      if (split_workspace(stream, sm_count, s2)) st = s2;
+      if (std::getenv("B200_GEMM_DEBUG"))
+        std::fprintf(stderr, "b200_gemm: %lld tiles on %d pairs, last %lld tiles split %d ways%s\n", tiles, grid_pairs,
+                     r, S, st.S > 1 ? "" : " (no workspace: unsplit)");
+    }
+  }
   const cudaError_t le = launch_gemm(kern, dim3(2 * grid_pairs), dim3(kThreads), Cfg::kSmemBytes, stream, ta, tb, tc,
-                                     M, N, K, group_m, g.scale);
+                                     M, N, K, group_m, g.scale, st);
   return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -389,8 +497,10 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
   double best_cost = 1e300;
   for (const Opt& o : opts) {
     const long long tiles = (long long)((m + o.tile_m - 1) / o.tile_m) * ((n + o.tile_n - 1) / o.tile_n);
-    const long long waves = (tiles + o.slots - 1) / o.slots;
-    const double cost = (double)waves * o.per_sm_work / o.rate;
+    double waves = (double)((tiles + o.slots - 1) / o.slots);
+    if (o.variant == B200_VARIANT_PAIR && split_enabled() && tiles % o.slots != 0)
+      waves = (double)(tiles / o.slots) + pair_tail_fraction((k + 127) / 128, tiles, o.slots);  // split last wave
+    const double cost = waves * o.per_sm_work / o.rate;
     if (cost < best_cost * 0.999) {
       best_cost = cost;
       best = o.variant;

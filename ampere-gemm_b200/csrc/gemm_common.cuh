@@ -294,4 +294,78 @@ __host__ __device__ __forceinline__ float ordered_to_float(uint32_t u) {
   return f;
 }
 
+// ---------------------------------------------------------------------------
+// Split of the last, partial wave along K (2-CTA pair kernel, 256 x 256
+// tiles).  A persistent kernel runs whole tiles in waves of `slots` pairs; when
+// the last wave holds only R < slots tiles, those R tiles are cut into S
+// K-ranges each (R * S <= slots units, one per pair), so the last wave takes
+// about 1/S of a tile instead of a whole one.  Each unit writes its fp32 part
+// (per CTA: 128 x 256) to a private workspace and bumps the tile's counter;
+// the unit that arrives last sums the S parts in the fixed order 0..S-1 (its
+// own from TMEM) and stores C through the normal epilogue.  No unit waits for
+// another, and the result does not depend on the order of arrival.
+// ---------------------------------------------------------------------------
+struct SplitTail {
+  int dp_tiles = 0x7fffffff;       // tiles [0, dp_tiles) run whole, in full waves
+  int S = 1;                       // K ranges per tail tile (1: no split)
+  float* ws = nullptr;             // parts: [tail tile][S][CTA of the pair], kPartFloats each
+  uint32_t* counters = nullptr;    // [tail tile][CTA of the pair]: (seq << 8) | arrivals
+  uint32_t seq = 1;                // launch tag, never 0
+};
+
+constexpr int kPartFloats = 128 * 256;  // one CTA's share of a 256 x 256 tile
+
+struct WorkUnit {
+  int t;         // tile index (raster order)
+  int kb0, kb1;  // K blocks [kb0, kb1)
+  int s;         // K range of a tail tile, or -1 for a whole tile
+};
+
+// Unit number `it` of pair `slot` (of `num_slots`); false when it has none.
+__device__ __forceinline__ bool work_unit(int it, int slot, int num_slots, int num_tiles, int num_kb,
+                                          const SplitTail& st, WorkUnit& u) {
+  const int full = (st.S <= 1) ? 0x7fffffff : st.dp_tiles / num_slots;
+  if (it < full) {
+    u.t = slot + it * num_slots;
+    u.kb0 = 0;
+    u.kb1 = num_kb;
+    u.s = -1;
+    return u.t < num_tiles;
+  }
+  if (it > full || slot >= (num_tiles - st.dp_tiles) * st.S) return false;
+  u.t = st.dp_tiles + slot / st.S;
+  u.s = slot % st.S;
+  u.kb0 = static_cast<int>(static_cast<long long>(u.s) * num_kb / st.S);
+  u.kb1 = static_cast<int>(static_cast<long long>(u.s + 1) * num_kb / st.S);
+  return true;
+}
+
+// Float offset of lane `lane`'s float4 number q of 64-column chunk c of TMEM
+// quadrant `quad` inside one part: consecutive lanes are consecutive 16-byte
+// words, so every warp-wide access moves 512 contiguous bytes.
+__device__ __forceinline__ int part_offset(int quad, int c, int q, int lane) {
+  return (((quad * 4 + c) * 16 + q) * 32 + lane) * 4;
+}
+
+// Counts this unit's arrival at its tail tile; true for the last of S.  The
+// retry loop only repeats when another arrival won the race (at most S - 1
+// times); its bound is a safeguard.
+__device__ __forceinline__ bool split_arrive_last(uint32_t* ctr, uint32_t seq, int S) {
+  uint32_t cur = atomicAdd(ctr, 0u);
+  for (int i = 0; i < 4096; ++i) {
+    const uint32_t next = ((cur >> 8) == seq) ? cur + 1u : ((seq << 8) | 1u);
+    const uint32_t old = atomicCAS(ctr, cur, next);
+    if (old == cur) return (next & 0xffu) == static_cast<uint32_t>(S);
+    cur = old;
+  }
+  raise_device_error(kDevTimeoutEpilogue);
+  return false;
+}
+
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
 }  // namespace b200

@@ -26,6 +26,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
 
   B200_PROF_DECL
+#ifdef B200_GEMM_PROFILE
+  // Timeline of one launch (profile build): entry time, then per role the
+  // nanoseconds from entry to the first data / the end of the epilogue.
+  const uint64_t prof_entry = global_timer_ns();
+  bool prof_first = true;
+#endif
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -147,6 +153,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
+#ifdef B200_GEMM_PROFILE
+          if (prof_first) { B200_PROF_ADD(6, global_timer_ns() - prof_entry); prof_first = false; }
+#endif
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
@@ -228,6 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();
+#ifdef B200_GEMM_PROFILE
+    B200_PROF_ADD(5, prof_entry);
+    B200_PROF_ADD(7, global_timer_ns() - prof_entry);
+#endif
   }
 
   B200_PROF_FLUSH

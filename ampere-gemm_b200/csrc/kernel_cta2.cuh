@@ -56,7 +56,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
-                                 const __grid_constant__ EpiParams sc) {
+                                 const __grid_constant__ EpiParams sc, const __grid_constant__ SplitTail st) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
   constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -72,6 +72,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* mma_drain = tmem_empty + kAcc * MSUB;     // [1]      abort path only
   uint64_t* c_bar = mma_drain + 1;                    // [4]      old-C loads of the epilogue warps (beta != 0)
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(c_bar + kEpiWarps);
+  uint32_t* split_last = tmem_base_slot + 1;          // split tail: this CTA's unit arrived last
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -126,12 +127,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+      WorkUnit u;
+      for (int it = 0; ok && work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it) {
         int mb, nb;
-        sched.tile_coords(t, mb, nb);
+        sched.tile_coords(u.t, mb, nb);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * (kBM * MSUB);
         const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
 #ifdef B200_GEMM_NOLOAD
           if (leader) mbar_arrive(&full_bar[stage]);
@@ -199,10 +201,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #ifdef B200_GEMM_PROFILE
       const long long prof_t0 = clock64();
 #endif
-      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++local) {
+      WorkUnit u;
+      for (int it = 0; ok && work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it, ++local) {
         const int buf = local % kAcc;
         const uint32_t acc_phase = (local / kAcc) & 1;
-        for (int kb = 0; kb < num_kb && ok; ++kb) {
+        for (int kb = u.kb0; kb < u.kb1 && ok; ++kb) {
           if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
@@ -217,7 +220,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
 #pragma unroll
             for (int s = 0; s < MSUB; ++s) {
-              if (kb == 0 && k == 0) {
+              if (kb == u.kb0 && k == 0) {
                 // First write of this 256-column block in the tile: the
                 // epilogue must have drained it (both CTAs).
                 if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + s], acc_phase ^ 1u, kDevTimeoutMma))) {
@@ -232,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                       : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
               const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
 #ifndef B200_GEMM_NOMMA
-              umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+              umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
 #endif
               any_mma = true;
             }
@@ -264,9 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int sbuf = 0;
     uint32_t c_phase = 0;
     int local = 0;
-    for (int t = pair; t < num_tiles; t += num_pairs, ++local) {
+    WorkUnit u;
+    for (int it = 0; work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it, ++local) {
       int mb, nb;
-      sched.tile_coords(t, mb, nb);
+      sched.tile_coords(u.t, mb, nb);
       const int n0 = nb * Cfg::kTileN;
       const int buf = local % kAcc;
       const uint32_t acc_phase = (local / kAcc) & 1;
@@ -286,6 +290,85 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
         continue;
 #endif
+        if (MSUB == 1 && u.s >= 0) {
+          // Tail unit of a split tile: publish this K range's part, and if it
+          // is the last to arrive, sum all parts and store the tile.
+#ifdef B200_GEMM_PROFILE
+          const uint64_t prof_s0 = global_timer_ns();
+#endif
+          const int tail = u.t - st.dp_tiles;
+          float* part0 = st.ws + static_cast<size_t>(tail * st.S * 2 + static_cast<int>(rank)) * kPartFloats;
+          const size_t part_stride = 2 * static_cast<size_t>(kPartFloats);   // next K range, same CTA
+#pragma unroll 1
+          for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+            uint32_t lo[32], hi[32];
+            tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
+            tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
+            tmem_ld_wait_regs(lo);
+            tmem_ld_wait_regs(hi);
+            float* dst = part0 + u.s * part_stride;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const uint32_t* v = (q < 8) ? (lo + 4 * q) : (hi + 4 * (q - 8));
+              *reinterpret_cast<float4*>(dst + part_offset(quad, c, q, lane)) =
+                  make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]),
+                              __uint_as_float(v[3]));
+            }
+          }
+          __threadfence();
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+          if (threadIdx.x == 64) *split_last = split_arrive_last(st.counters + tail * 2 + rank, st.seq, st.S) ? 1u : 0u;
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+#ifdef B200_GEMM_PROFILE
+          const uint64_t prof_s1 = global_timer_ns();
+          B200_PROF_ADD(5, prof_s1 - prof_s0);
+          B200_PROF_ADD(7, 1);
+#endif
+          if (*reinterpret_cast<volatile uint32_t*>(split_last)) {
+            __threadfence();
+#pragma unroll 1
+            for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+              uint32_t lo[32], hi[32];
+              tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
+              tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
+              tmem_ld_wait_regs(lo);
+              tmem_ld_wait_regs(hi);
+              float acc[64];
+#pragma unroll 1
+              for (int r = 0; r < st.S; ++r) {
+                const float* src = part0 + r * part_stride;
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                  const uint32_t* own = (q < 8) ? (lo + 4 * q) : (hi + 4 * (q - 8));
+                  const float4 v = (r == u.s) ? make_float4(__uint_as_float(own[0]), __uint_as_float(own[1]),
+                                                            __uint_as_float(own[2]), __uint_as_float(own[3]))
+                                              : ld_cg_f4(src + part_offset(quad, c, q, lane));
+                  if (r == 0) {
+                    acc[4 * q] = v.x; acc[4 * q + 1] = v.y; acc[4 * q + 2] = v.z; acc[4 * q + 3] = v.w;
+                  } else {
+                    acc[4 * q] += v.x; acc[4 * q + 1] += v.y; acc[4 * q + 2] += v.z; acc[4 * q + 3] += v.w;
+                  }
+                }
+              }
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                lo[e] = __float_as_uint(acc[e]);
+                hi[e] = __float_as_uint(acc[32 + e]);
+              }
+              epi_store_block<2>(&tmap_c, epi_buf, epi_addr, sbuf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32,
+                                 sc, &c_bar[ew], c_phase);
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+            if (threadIdx.x == 64) atomicExch(st.counters + tail * 2 + rank, 0u);  // ready for the next launch
+#ifdef B200_GEMM_PROFILE
+            B200_PROF_ADD(6, global_timer_ns() - prof_s1);
+#endif
+          }
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
+          continue;
+        }
 #pragma unroll 1
         for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
           uint32_t lo[32], hi[32];
