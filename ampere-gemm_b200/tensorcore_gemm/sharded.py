@@ -114,10 +114,33 @@ class GatheredOutput:
         self.ldc = max(8, -(-self.N // 8) * 8)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         with torch.cuda.device(self.device):
-            self._ptr, handle = _native.ipc_alloc(max(1, self.M) * self.ldc * 2)
+            try:
+                self._ptr, handle = _native.ipc_alloc(max(1, self.M) * self.ldc * 2)
+            except RuntimeError:
+                self._ptr, handle = 0, b""
             handles = [None] * self.world
             dist.all_gather_object(handles, handle, group=group)
-            self._peers = [_native.ipc_open(h) for r, h in enumerate(handles) if r != self.rank]
+            self._peers, failure = [], None
+            if not all(handles):
+                failure = "a rank could not allocate its IPC buffer"
+            else:
+                try:
+                    for r, h in enumerate(handles):
+                        if r != self.rank:
+                            self._peers.append(_native.ipc_open(h))
+                except RuntimeError as exc:
+                    failure = str(exc)
+            # Every rank learns whether all succeeded, so they fail together
+            # and no rank is left waiting in a later collective.
+            flag = torch.tensor([1.0 if failure else 0.0], device=self.device)
+            dist.all_reduce(flag, group=group)
+            if flag.item() > 0:
+                for p in self._peers:
+                    _native.ipc_close(p)
+                dist.barrier(group=group)
+                if self._ptr:
+                    _native.ipc_free(self._ptr)
+                raise RuntimeError(f"gathered output unavailable: {failure or 'failed on another rank'}")
             self._buf = _DeviceBuffer(self._ptr, max(1, self.M), self.ldc)
             self._full = torch.as_tensor(self._buf, device=self.device)
             self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)

@@ -567,8 +567,19 @@ def run_b200(args) -> int:
 
     gathered = None
     if world > 1 and not args.no_extras:
-        gathered = gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank, barrier,
-                                               max_over_ranks, ms_max / args.steps)
+        # A side measurement: whatever goes wrong here must not cost the main
+        # line.  Every rank agrees on success before the result is used.
+        try:
+            gathered = gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank, barrier,
+                                                   max_over_ranks, ms_max / args.steps)
+            err = None
+        except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+            err = f"{type(exc).__name__}: {exc}"[:300]
+        bad = torch.tensor([1.0 if err else 0.0], device=dev)
+        dist.all_reduce(bad)
+        if bad.item() > 0:
+            gathered = {"unavailable": err or "failed on another rank"}
+        torch.cuda.synchronize()
 
     extras = None
     cpu = None
