@@ -289,20 +289,27 @@ int max_active_pairs(Kern kern, int smem_bytes, int sm_count) {
 
 // ---- split of the last wave along K (pair kernel, MSUB = 1) ----
 // Cost model in SM cycles: a 256 x 256 pair tile spends 1024 cycles per
-// 128-deep K stage.  A split tail costs about 12.4k cycles for writing the
-// unit's 128 KB part and arriving, plus 3k per K range for the last unit's
-// read-back and sum (profile build, 1.9 GHz: 3.7-4.0 us per part write, 5.6 us
-// fixup at S = 2, 7.1-7.4 us at S = 3).  So only deep K pays: at K <= 4096 the
-// last wave stays whole.
+// 128-deep K stage.  A split tail costs about 8.1k cycles plus 3.4k per K
+// range (writing the parts, the arrival, the last unit's read-back and sum),
+// fitted to 2560 x 2048 x 8192 at S = 2, 3, 4, 7 (saved time against the
+// ideal T (1 - 1/S)).  So only deep K pays: at K = 2048 the split is slower,
+// at K = 4096 even, at K = 8192 S = 4 saves 16 %.
 constexpr double kPairStageCycles = 1024.0;
-constexpr double kSplitFixedCycles = 12400.0;
-constexpr double kSplitPartCycles = 3000.0;
+constexpr double kSplitFixedCycles = 8100.0;
+constexpr double kSplitPartCycles = 3400.0;
 
 // K ranges per tail tile that minimise the last wave's time (1 = no split).
 int choose_split(int num_kb, long long smax) {
+  // B200_GEMM_SPLIT_S forces the number of K ranges (tuning only).
+  static const int forced = [] {
+    const char* e = std::getenv("B200_GEMM_SPLIT_S");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced >= 1) return (int)std::max<long long>(1, std::min<long long>({(long long)forced, smax, kFixBufs + 1,
+                                                                         num_kb / 2}));
   int best = 1;
   double best_cost = num_kb * kPairStageCycles;
-  for (int S = 2; S <= smax && S <= 16 && 2 * S <= num_kb; ++S) {
+  for (int S = 2; S <= smax && S <= kFixBufs + 1 && 2 * S <= num_kb; ++S) {  // fixup holds S - 1 parts
     const double c = num_kb * kPairStageCycles / S + kSplitFixedCycles + kSplitPartCycles * S;
     if (c < best_cost * 0.97) {
       best_cost = c;
@@ -340,7 +347,6 @@ struct SplitWorkspace {
   float* parts;
   uint32_t* counters;
   int max_parts;
-  uint32_t seq;
 };
 
 std::mutex g_split_mu;
@@ -371,13 +377,22 @@ bool split_workspace(cudaStream_t stream, int sm_count, SplitTail& st) {
       return false;
     }
     w = &g_split_ws[g_split_n++];
-    *w = SplitWorkspace{dev, stream, static_cast<float*>(mem), ctr, max_parts, 0};
+    *w = SplitWorkspace{dev, stream, static_cast<float*>(mem), ctr, max_parts};
   }
-  w->seq = (w->seq % 0xffffffu) + 1u;  // 1 .. 2^24 - 1
   st.ws = w->parts;
   st.counters = w->counters;
-  st.seq = w->seq;
   return true;  // R * S <= pairs <= sm_count / 2, so the parts always fit
+}
+
+// Zeroes the tail counters of every workspace on the current device (after a
+// launch that gave up on a bounded wait; the device is idle then).
+void reset_split_counters() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(g_split_mu);
+  for (int i = 0; i < g_split_n; ++i)
+    if (g_split_ws[i].dev == dev)
+      (void)cudaMemset(g_split_ws[i].counters, 0, (size_t)g_split_ws[i].max_parts * sizeof(uint32_t));
 }
 
 template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
@@ -812,6 +827,7 @@ extern "C" int b200_gemm_last_device_error(void) {
   if (cudaMemcpyFromSymbol(&v, b200::g_device_error, sizeof(int)) != cudaSuccess) return -1;
   const int zero = 0;
   if (v != 0 && cudaMemcpyToSymbol(b200::g_device_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) b200::reset_split_counters();  // an aborted launch may have left tail counters counting
   return v;
 }
 
@@ -824,6 +840,15 @@ extern "C" int b200_gemm_sm_count(void) {
 extern "C" int b200_gemm_version(void) { return 101; }
 
 #ifdef B200_GEMM_PROFILE
+// Copies and clears the per-CTA split-tail step timestamps (profiling builds only).
+extern "C" __attribute__((visibility("default"))) int b200_gemm_debug_read_split_profile(unsigned long long* host,
+                                                                                       int rows) {
+  if (rows > 1024) rows = 1024;
+  if (cudaMemcpyFromSymbol(host, b200::g_split_prof, sizeof(unsigned long long) * 8 * rows) != cudaSuccess) return -1;
+  static unsigned long long zero[1024][8];
+  return cudaMemcpyToSymbol(b200::g_split_prof, zero, sizeof(zero)) == cudaSuccess ? 0 : -1;
+}
+
 // Copies and clears the per-CTA wait counters (profiling builds only).
 extern "C" __attribute__((visibility("default"))) int b200_gemm_debug_read_profile(unsigned long long* host, int rows) {
   if (rows > 1024) rows = 1024;

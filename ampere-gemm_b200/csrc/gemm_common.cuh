@@ -24,6 +24,10 @@ __device__ unsigned long long g_prof[1024][8];
     _r;                                          \
   })
 #define B200_PROF_ADD(slot, v) (prof_acc[slot] += (unsigned long long)(v))
+// Split-tail step timestamps (ns since the unit's start), one row per CTA.
+__device__ unsigned long long g_split_prof[1024][8];
+#define B200_SPLIT_MARK(i, t0) \
+  if (threadIdx.x == 64) g_split_prof[blockIdx.x & 1023][i] = global_timer_ns() - (t0)
 #define B200_PROF_FLUSH                                                         \
   if (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64) {             \
     for (int _i = 0; _i < 8; ++_i)                                              \
@@ -33,6 +37,7 @@ __device__ unsigned long long g_prof[1024][8];
 #define B200_PROF_DECL
 #define B200_TIMED(slot, expr) (expr)
 #define B200_PROF_ADD(slot, v) ((void)0)
+#define B200_SPLIT_MARK(i, t0) ((void)0)
 #define B200_PROF_FLUSH
 #endif
 
@@ -309,8 +314,7 @@ struct SplitTail {
   int dp_tiles = 0x7fffffff;       // tiles [0, dp_tiles) run whole, in full waves
   int S = 1;                       // K ranges per tail tile (1: no split)
   float* ws = nullptr;             // parts: [tail tile][S][CTA of the pair], kPartFloats each
-  uint32_t* counters = nullptr;    // [tail tile][CTA of the pair]: (seq << 8) | arrivals
-  uint32_t seq = 1;                // launch tag, never 0
+  uint32_t* counters = nullptr;    // [tail tile][CTA of the pair]: arrivals so far (0 between launches)
 };
 
 constexpr int kPartFloats = 128 * 256;  // one CTA's share of a 256 x 256 tile
@@ -348,24 +352,12 @@ __device__ __forceinline__ int part_offset(int quad, int c, int q, int lane) {
 }
 
 // Counts this unit's arrival at its tail tile; true for the last of S.  The
-// retry loop only repeats when another arrival won the race (at most S - 1
-// times); its bound is a safeguard.
-__device__ __forceinline__ bool split_arrive_last(uint32_t* ctr, uint32_t seq, int S) {
-  uint32_t cur = atomicAdd(ctr, 0u);
-  for (int i = 0; i < 4096; ++i) {
-    const uint32_t next = ((cur >> 8) == seq) ? cur + 1u : ((seq << 8) | 1u);
-    const uint32_t old = atomicCAS(ctr, cur, next);
-    if (old == cur) return (next & 0xffu) == static_cast<uint32_t>(S);
-    cur = old;
-  }
-  raise_device_error(kDevTimeoutEpilogue);
-  return false;
+// last arrival resets the counter to 0 once the tile is stored, so every
+// launch finds its counters at 0 (the library clears them after a launch that
+// raised the device error word).
+__device__ __forceinline__ bool split_arrive_last(uint32_t* ctr, int S) {
+  return atomicAdd(ctr, 1u) == static_cast<uint32_t>(S - 1);
 }
 
-__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-  return v;
-}
 
 }  // namespace b200

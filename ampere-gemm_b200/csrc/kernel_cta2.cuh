@@ -30,6 +30,11 @@
 
 namespace b200 {
 
+// Split-tail fixup: per epilogue warp, kFixBufs 8 KB buffers (one 32 x 64
+// fp32 chunk each) carved from the pipeline stages, which are idle by then.
+constexpr int kFixBufs = 6;
+constexpr uint32_t kEpiChunkF32Bytes = kEpiRows * kEpiCols * 4;  // 8 KB
+
 template <int STAGES, int KSUB, int MSUB>
 struct PairConfig {
   static constexpr int kStageK = kBK * KSUB;         // K per stage (KSUB swizzle atoms)
@@ -45,10 +50,12 @@ struct PairConfig {
   static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
   static constexpr int kAccBufs = (MSUB == 1) ? 2 : 1;  // tiles resident in TMEM
   static constexpr int kTmemCols = 512;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 256 + 1024;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 512 + 1024;
   static_assert(kAccBufs * MSUB * kTileN <= kTmemCols, "accumulators exceed TMEM");
   static_assert(MSUB * KSUB * (kBK / kUmmaK) >= 8, "a pair stage needs at least 8 MMAs");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
+  static_assert(MSUB != 1 || STAGES * kStageBytes >= kEpiWarps * kFixBufs * (int)kEpiChunkF32Bytes,
+                "split-tail fixup buffers must fit in the pipeline stages");
 };
 
 template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
@@ -71,7 +78,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* tmem_empty = bars + 2 * STAGES + kAcc;    // [kAcc * MSUB] leader: one 256-column block drained
   uint64_t* mma_drain = tmem_empty + kAcc * MSUB;     // [1]      abort path only
   uint64_t* c_bar = mma_drain + 1;                    // [4]      old-C loads of the epilogue warps (beta != 0)
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(c_bar + kEpiWarps);
+  uint64_t* fix_bar = c_bar + kEpiWarps;              // [4 x kFixBufs] split-tail fixup loads, per epilogue warp
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(fix_bar + kEpiWarps * kFixBufs);
   uint32_t* split_last = tmem_base_slot + 1;          // split tail: this CTA's unit arrived last
 
   B200_PROF_DECL
@@ -101,6 +109,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int a = 0; a < kAcc * MSUB; ++a) mbar_init(&tmem_empty[a], 2 * kEpiWarps);
     mbar_init(mma_drain, 1);
     for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
+    for (int e = 0; e < kEpiWarps * kFixBufs; ++e) mbar_init(&fix_bar[e], 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -292,42 +301,83 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #endif
         if (MSUB == 1 && u.s >= 0) {
           // Tail unit of a split tile: publish this K range's part, and if it
-          // is the last to arrive, sum all parts and store the tile.
+          // is the last to arrive, sum all parts and store the tile.  Parts
+          // move as 8 KB bulk copies ([quad][chunk] blocks of [q][lane]
+          // float4) staged in this warp's share of the pipeline stages, which
+          // are idle once the tail unit's MMAs have completed.
 #ifdef B200_GEMM_PROFILE
           const uint64_t prof_s0 = global_timer_ns();
 #endif
           const int tail = u.t - st.dp_tiles;
           float* part0 = st.ws + static_cast<size_t>(tail * st.S * 2 + static_cast<int>(rank)) * kPartFloats;
           const size_t part_stride = 2 * static_cast<size_t>(kPartFloats);   // next K range, same CTA
+          uint8_t* fix_buf = smem + ew * (kFixBufs * kEpiChunkF32Bytes);   // kFixBufs x 8 KB
+          uint64_t* fbar = fix_bar + ew * kFixBufs;
+          constexpr int kChunks = Cfg::kTileN / kEpiCols;                   // 4
+          static_assert(kChunks <= kFixBufs, "a part's chunks must fit the warp's buffers");
 #pragma unroll 1
-          for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t lo[32], hi[32];
             tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
             tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
             tmem_ld_wait_regs(lo);
             tmem_ld_wait_regs(hi);
-            float* dst = part0 + u.s * part_stride;
+            float* stage_f = reinterpret_cast<float*>(fix_buf + c * kEpiChunkF32Bytes);
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
               const uint32_t* v = (q < 8) ? (lo + 4 * q) : (hi + 4 * (q - 8));
-              *reinterpret_cast<float4*>(dst + part_offset(quad, c, q, lane)) =
-                  make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]),
-                              __uint_as_float(v[3]));
+              st_shared_v4(smem_u32(stage_f + (q * 32 + lane) * 4), v[0], v[1], v[2], v[3]);
             }
           }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int c = 0; c < kChunks; ++c)
+              bulk_store_s2g(part0 + u.s * part_stride + part_offset(quad, c, 0, 0), fix_buf + c * kEpiChunkF32Bytes,
+                             kEpiChunkF32Bytes);
+            bulk_commit_group();
+            bulk_wait_group<0>();        // the part is in global memory
+            fence_proxy_async_global();
+          }
+          B200_SPLIT_MARK(0, prof_s0);
+          __syncwarp();
           __threadfence();
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-          if (threadIdx.x == 64) *split_last = split_arrive_last(st.counters + tail * 2 + rank, st.seq, st.S) ? 1u : 0u;
+          B200_SPLIT_MARK(3, prof_s0);
+          if (threadIdx.x == 64) *split_last = split_arrive_last(st.counters + tail * 2 + rank, st.S) ? 1u : 0u;
+          B200_SPLIT_MARK(4, prof_s0);
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+          B200_SPLIT_MARK(5, prof_s0);
 #ifdef B200_GEMM_PROFILE
           const uint64_t prof_s1 = global_timer_ns();
           B200_PROF_ADD(5, prof_s1 - prof_s0);
           B200_PROF_ADD(7, 1);
 #endif
           if (*reinterpret_cast<volatile uint32_t*>(split_last)) {
+            // The S - 1 other parts stream through the kFixBufs-buffer ring,
+            // up to kFixBufs 8 KB loads in flight: load L (chunk L / (S-1))
+            // uses buffer L % kFixBufs, phase (L / kFixBufs) & 1.
             __threadfence();
+            fence_proxy_async_global();
+            const int others = st.S - 1;
+            const int total = kChunks * others;
+            int issued = 0;
+            auto issue_upto = [&](int limit) {
+              if (lane == 0) {
+                for (int L = issued; L < limit && L < total; ++L) {
+                  const int c = L / others, i = L % others;
+                  const int r = i < u.s ? i : i + 1;  // the other K ranges in order
+                  mbar_arrive_expect_tx(&fbar[L % kFixBufs], kEpiChunkF32Bytes);
+                  bulk_load_g2s(fix_buf + (L % kFixBufs) * kEpiChunkF32Bytes,
+                                part0 + r * part_stride + part_offset(quad, c, 0, 0), kEpiChunkF32Bytes,
+                                &fbar[L % kFixBufs]);
+                }
+              }
+              issued = limit < total ? limit : total;
+            };
+            issue_upto(kFixBufs);
 #pragma unroll 1
-            for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+            for (int c = 0; c < kChunks; ++c) {
               uint32_t lo[32], hi[32];
               tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
               tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
@@ -336,13 +386,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               float acc[64];
 #pragma unroll 1
               for (int r = 0; r < st.S; ++r) {
-                const float* src = part0 + r * part_stride;
+                const float* src = nullptr;
+                if (r != u.s) {
+                  const int L = c * others + (r < u.s ? r : r - 1);
+                  mbar_wait(&fbar[L % kFixBufs], static_cast<uint32_t>((L / kFixBufs) & 1), kDevTimeoutEpilogue);
+                  src = reinterpret_cast<const float*>(fix_buf + (L % kFixBufs) * kEpiChunkF32Bytes);
+                }
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
                   const uint32_t* own = (q < 8) ? (lo + 4 * q) : (hi + 4 * (q - 8));
-                  const float4 v = (r == u.s) ? make_float4(__uint_as_float(own[0]), __uint_as_float(own[1]),
-                                                            __uint_as_float(own[2]), __uint_as_float(own[3]))
-                                              : ld_cg_f4(src + part_offset(quad, c, q, lane));
+                  float4 v;
+                  if (src) {
+                    v = *reinterpret_cast<const float4*>(src + (q * 32 + lane) * 4);
+                  } else {
+                    v = make_float4(__uint_as_float(own[0]), __uint_as_float(own[1]), __uint_as_float(own[2]),
+                                    __uint_as_float(own[3]));
+                  }
                   if (r == 0) {
                     acc[4 * q] = v.x; acc[4 * q + 1] = v.y; acc[4 * q + 2] = v.z; acc[4 * q + 3] = v.w;
                   } else {
@@ -350,6 +409,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                   }
                 }
               }
+              __syncwarp();                            // this chunk's buffers are free again
+              issue_upto((c + 1) * others + kFixBufs);
+              if (c == 0) B200_SPLIT_MARK(6, prof_s0);
 #pragma unroll
               for (int e = 0; e < 32; ++e) {
                 lo[e] = __float_as_uint(acc[e]);
@@ -360,6 +422,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
             if (threadIdx.x == 64) atomicExch(st.counters + tail * 2 + rank, 0u);  // ready for the next launch
+            B200_SPLIT_MARK(7, prof_s0);
 #ifdef B200_GEMM_PROFILE
             B200_PROF_ADD(6, global_timer_ns() - prof_s1);
 #endif
