@@ -253,7 +253,7 @@ def run_reference(args):
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -617,7 +617,7 @@ def run_b200(args) -> int:
             line["extras"] = extras
         if gathered is not None:
             line["gathered_output"] = gathered
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -664,15 +664,34 @@ def run_case(args) -> int:
         f(i)
     ms = _time_graph(torch, f, args.steps) if args.graph else _time_launches(torch, f, args.steps)
     err = _native.last_device_error()
-    print(json.dumps({"case": args.case, "variant": args.variant, "dist": args.dist, "graph": args.graph,
+    emit({"case": args.case, "variant": args.variant, "dist": args.dist, "graph": args.graph,
                       "us": round(ms * 1e3, 2),
                       "TFLOPs": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
                       "GBps": round(set_bytes / (ms * 1e-3) / 1e9, 1), "operand_sets": nsets,
-                      "device_error_word": err}), flush=True)
+                      "device_error_word": err})
     return 0 if err == 0 else 1
 
 
+# The result line goes to the process's original stdout; everything else that
+# writes to file descriptor 1 (NCCL's version banner, library logs) is sent to
+# stderr, so stdout carries exactly one JSON line.
+RESULT_OUT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    print(json.dumps(line), file=RESULT_OUT, flush=True)
+
+
+def _isolate_stdout() -> None:
+    global RESULT_OUT
+    sys.stdout.flush()
+    RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+
 def main() -> int:
+    _isolate_stdout()
     args = parse_args()
     if args.case:
         return run_case(args)
