@@ -214,7 +214,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int it = 0; ok && work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it, ++local) {
         const int buf = local % kAcc;
         const uint32_t acc_phase = (local / kAcc) & 1;
-        for (int kb = u.kb0; kb < u.kb1 && ok; ++kb) {
+        // The MMAs of one K step: 256-column block s of this tile's accumulator.
+        auto issue_block = [&](int stg, int kb, int s) {
+          const uint32_t a_addr = a_base + stg * Cfg::kABytes;
+          const uint32_t b_addr = b_base + stg * Cfg::kBBytes;
+#pragma unroll
+          for (int k = 0; k < Cfg::kStageK / kUmmaK; ++k) {
+            const int sub = k / (kBK / kUmmaK), j = k % (kBK / kUmmaK);
+            uint64_t bdesc;
+            if constexpr (kBRowMajor)
+              bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), Cfg::kBPanel);
+            else
+              bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
+            const uint64_t adesc =
+                kAColMajor ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
+                           : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
+            const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
+#ifndef B200_GEMM_NOMMA
+            umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
+#endif
+          }
+          any_mma = true;
+        };
+        int kb_first = u.kb0;
+        if constexpr (MSUB == 2) {
+          // Tile start: the previous tile's two 256-column blocks are drained
+          // one after the other.  Run the first P stages into block 0 alone
+          // (they stay resident), then, once block 1 is free, the same stages
+          // into block 1, and release them: the tensor pipe works while
+          // block 1 drains instead of waiting for both.
+          const int P = (u.kb1 - u.kb0) < STAGES ? (u.kb1 - u.kb0) : STAGES;
+          if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + 0], acc_phase ^ 1u, kDevTimeoutMma))) {
+            ok = false;
+          }
+          tc_fence_after_sync();
+          int stg = stage;
+          uint32_t ph = phase;
+          for (int j = 0; j < P && ok; ++j) {
+            if (!B200_TIMED(2, mbar_wait(&full_bar[stg], ph, kDevTimeoutMma))) { ok = false; break; }
+            tc_fence_after_sync();
+            issue_block(stg, u.kb0 + j, 0);
+            if (++stg == STAGES) { stg = 0; ph ^= 1u; }
+          }
+          if (ok && !B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + 1], acc_phase ^ 1u, kDevTimeoutMma)))
+            ok = false;
+          if (!ok) break;
+          tc_fence_after_sync();
+          for (int j = 0; j < P; ++j) {
+            issue_block(stage, u.kb0 + j, 1);
+            const uint32_t e = smem_u32(&empty_bar[stage]);
+            umma_commit_cta2(e);
+            umma_commit_cta2(mapa_shared(e, 1));
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          }
+          kb_first = u.kb0 + P;
+        }
+        for (int kb = kb_first; kb < u.kb1 && ok; ++kb) {
           if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
@@ -229,7 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
 #pragma unroll
             for (int s = 0; s < MSUB; ++s) {
-              if (kb == u.kb0 && k == 0) {
+              if (MSUB == 1 && kb == u.kb0 && k == 0) {
                 // First write of this 256-column block in the tile: the
                 // epilogue must have drained it (both CTAs).
                 if (!B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + s], acc_phase ^ 1u, kDevTimeoutMma))) {
