@@ -338,6 +338,13 @@ bool split_enabled() {
   return on;
 }
 
+// K ranges the 256 x 256 pair kernel cuts its last wave into (1 = none) for
+// `tiles` tiles on `grid_pairs` resident pairs and `num_kb` 128-deep K stages.
+int split_ranges_for(long long tiles, int grid_pairs, int num_kb) {
+  if (!split_enabled() || grid_pairs <= 0 || tiles <= grid_pairs || tiles % grid_pairs == 0) return 1;
+  return choose_split(num_kb, grid_pairs / (tiles % grid_pairs));
+}
+
 // One workspace per (device, stream): launches on one stream are ordered, so
 // they can share it; other streams get their own.  Allocated on first use
 // (never during a stream capture: that launch then runs unsplit).
@@ -430,19 +437,16 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
   SplitTail st;
-  if (MSUB == 1 && split_enabled() && tiles > grid_pairs && tiles % grid_pairs != 0) {
-    const int num_kb = (K + Cfg::kStageK - 1) / Cfg::kStageK;
+  const int S = (MSUB == 1) ? split_ranges_for(tiles, grid_pairs, (K + Cfg::kStageK - 1) / Cfg::kStageK) : 1;
+  if (S >= 2) {
     const long long r = tiles % grid_pairs;
-    const int S = choose_split(num_kb, grid_pairs / r);
-    if (S >= 2) {
-      SplitTail s2;
-      s2.dp_tiles = (int)(tiles - r);
-      s2.S = S;
-      if (split_workspace(stream, sm_count, s2)) st = s2;
-      if (std::getenv("B200_GEMM_DEBUG"))
-        std::fprintf(stderr, "b200_gemm: %lld tiles on %d pairs, last %lld tiles split %d ways%s\n", tiles, grid_pairs,
-                     r, S, st.S > 1 ? "" : " (no workspace: unsplit)");
-    }
+    SplitTail s2;
+    s2.dp_tiles = (int)(tiles - r);
+    s2.S = S;
+    if (split_workspace(stream, sm_count, s2)) st = s2;
+    if (std::getenv("B200_GEMM_DEBUG"))
+      std::fprintf(stderr, "b200_gemm: %lld tiles on %d pairs, last %lld tiles split %d ways%s\n", tiles, grid_pairs, r,
+                   S, st.S > 1 ? "" : " (no workspace: unsplit)");
   }
   const cudaError_t le = launch_gemm(kern, dim3(2 * grid_pairs), dim3(kThreads), Cfg::kSmemBytes, stream, ta, tb, tc,
                                      M, N, K, group_m, g.scale, st);
@@ -498,16 +502,23 @@ int launch_skinny(const GemmArgs& g) {
 // 4000 x 6000 x 3000 and 65536 x 8192 x 8192.
 int pick_tensor_variant(int m, int n, int k, int sm_count) {
   if (k < 512) return B200_VARIANT_CTA1;  // a pair's prologue is not amortised
+  // One wave of 1-CTA tiles: every variant takes about one tile's time and the
+  // 1-CTA kernel has the cheapest start (2048^3: 16.4-16.7 us against 17.3-17.6
+  // for the pair kernel).
+  if ((long long)((m + 127) / 128) * ((n + 255) / 256) <= sm_count) return B200_VARIANT_CTA1;
+  // Cost in SM cycles: waves x one tile's MMA time / relative rate, plus the
+  // last tile's accumulator drain (one 256-column block, two for the wide pair).
   struct Opt {
-    int variant, tile_m, tile_n, slots;
-    double per_sm_work, rate;
+    int variant, tile_m, tile_n, slots, rows_per_sm;
+    double rate, drain_cycles;
   };
   const int pairs = sm_count / 2;
   const Opt opts[3] = {
-      {B200_VARIANT_PAIR_WIDE, 512, 256, pairs, 256.0 * 256.0, 1.00},
-      {B200_VARIANT_PAIR, 256, 256, pairs, 128.0 * 256.0, 0.96},
-      {B200_VARIANT_CTA1, 128, 256, sm_count, 128.0 * 256.0, 0.93},
+      {B200_VARIANT_PAIR_WIDE, 512, 256, pairs, 256, 1.00, 6400.0},
+      {B200_VARIANT_PAIR, 256, 256, pairs, 128, 0.96, 3200.0},
+      {B200_VARIANT_CTA1, 128, 256, sm_count, 128, 0.93, 3200.0},
   };
+  const double tile128_cycles = 8.0 * k;  // 128 x 256 rows x columns: k / 16 MMAs of 128 cycles
   int best = B200_VARIANT_CTA1;
   double best_cost = 1e300;
   for (const Opt& o : opts) {
@@ -515,13 +526,24 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
     double waves = (double)((tiles + o.slots - 1) / o.slots);
     if (o.variant == B200_VARIANT_PAIR && split_enabled() && tiles % o.slots != 0)
       waves = (double)(tiles / o.slots) + pair_tail_fraction((k + 127) / 128, tiles, o.slots);  // split last wave
-    const double cost = waves * o.per_sm_work / o.rate;
+    const double cost = waves * tile128_cycles * (o.rows_per_sm / 128.0) / o.rate + o.drain_cycles;
     if (cost < best_cost * 0.999) {
       best_cost = cost;
       best = o.variant;
     }
   }
   return best;
+}
+
+// The kernel the library runs for an m x n x k product when no variant is forced.
+int auto_variant(int m, int n, int k, int sm_count) {
+  if (k <= 256 && (n + 255) / 256 <= sm_count) {
+    // B-stationary pays for its one-off B load once a CTA has several tiles
+    // (measured: ahead from ~3 tiles per SM, behind at 1-2).
+    const long long tiles = (long long)((m + 127) / 128) * ((n + 255) / 256);
+    if (tiles >= 3LL * sm_count) return B200_VARIANT_SKINNY;
+  }
+  return pick_tensor_variant(m, n, k, sm_count);
 }
 
 // Process-wide kernel-variant override (b200_gemm_set_variant).
@@ -607,13 +629,7 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   ep.n_tma = n & ~7;  // a TMA store writes whole 16-byte pieces: the partial last one goes by plain stores
   const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, ep, dev.sm_count, stream};
   int variant = g_variant;
-  if (variant == B200_VARIANT_AUTO && k <= 256 && (n + 255) / 256 <= dev.sm_count) {
-    // B-stationary pays for its one-off B load once a CTA has several tiles
-    // (measured: ahead from ~3 tiles per SM, behind at 1-2).
-    const long long tiles = (long long)((m + 127) / 128) * ((n + 255) / 256);
-    if (tiles >= 3LL * dev.sm_count) variant = B200_VARIANT_SKINNY;
-  }
-  if (variant == B200_VARIANT_AUTO) variant = pick_tensor_variant(m, n, k, dev.sm_count);
+  if (variant == B200_VARIANT_AUTO) variant = auto_variant(m, n, k, dev.sm_count);
   if (variant == B200_VARIANT_SKINNY) {
     const int rc = with_layouts(row_b, col_a, [&](auto rb, auto ca) {
       // Measured: 5 A stages with 4 epilogue warps beat 4 stages with 8 warps
@@ -802,6 +818,23 @@ extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M
 extern "C" int b200_gemm_set_variant(int variant) {
   if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_PAIR_WIDE) return B200_ERR_INVALID_ARGUMENT;
   b200::g_variant = variant;
+  return B200_OK;
+}
+
+extern "C" int b200_gemm_plan(int64_t M, int64_t N, int64_t K, int sm_count, int* variant, int* k_ranges) {
+  using namespace b200;
+  if (M <= 0 || N <= 0 || K <= 0 || sm_count < 2 || !variant || !k_ranges) return B200_ERR_INVALID_ARGUMENT;
+  if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return B200_ERR_TOO_LARGE;
+  const int m = (int)M, n = (int)N, k = (int)K;
+  int v = g_variant != B200_VARIANT_AUTO ? g_variant : auto_variant(m, n, k, sm_count);
+  if (v == B200_VARIANT_SKINNY && (k > 256 || (n + 255) / 256 > sm_count)) v = B200_VARIANT_CTA1;
+  int ranges = 1;
+  if (v == B200_VARIANT_PAIR) {
+    const long long tiles = (long long)((m + 255) / 256) * ((n + 255) / 256);
+    ranges = split_ranges_for(tiles, (int)std::min<long long>(tiles, sm_count / 2), (k + 127) / 128);
+  }
+  *variant = v;
+  *k_ranges = ranges;
   return B200_OK;
 }
 

@@ -203,6 +203,14 @@ B200_API int b200_gemm_sm_count(void);
  * the B layout). */
 B200_API int b200_gemm_set_variant(int variant);
 
+/* The launch plan the library would use for an M x N x K product on a GPU
+ * with `sm_count` SMs (assuming sm_count / 2 resident 2-CTA clusters): the
+ * kernel variant (B200_VARIANT_*, honouring b200_gemm_set_variant) and, for
+ * B200_VARIANT_PAIR, the number of K ranges its partial last wave is split
+ * into (1 = none).  Host-only: touches no GPU.  No counterpart in the
+ * reference, whose mode string chose the kernel. */
+B200_API int b200_gemm_plan(int64_t M, int64_t N, int64_t K, int sm_count, int* variant, int* k_ranges);
+
 /* Self-test of the kernels' failure path: launches one thread that waits on
  * a barrier nothing arrives at, with a bounded wait of `limit_ns`
  * (1 ns .. 1 s), on the legacy default stream of the current device.  The

@@ -118,3 +118,38 @@ def test_gather_argument_validation_without_gpu(native_lib):
     assert lib.b200_ipc_alloc(0, ctypes.byref(ptr), buf) == _native.B200_ERR_INVALID_ARGUMENT
     assert lib.b200_ipc_open(None, ctypes.byref(ptr)) == _native.B200_ERR_INVALID_ARGUMENT
     assert lib.b200_ipc_close(None) == _native.B200_OK and lib.b200_ipc_free(None) == _native.B200_OK
+
+
+@pytest.mark.parametrize("shape,variant,ranges", [
+    ((65536, 8192, 8192), "pair2m", 1),   # bench workload, 1 GPU
+    ((8192, 8192, 8192), "pair2m", 1),    # its shard at 8 GPUs
+    ((32768, 1024, 256), "skinny", 1),    # K = 256, many tiles per SM
+    ((16384, 256, 256), "cta1", 1),       # K = 256, too few tiles for the B-stationary kernel
+    ((2048, 2048, 2048), "cta1", 1),      # one wave of 1-CTA tiles
+    ((200, 264, 136), "cta1", 1),         # K < 512
+    ((2560, 2048, 8192), "pair", 4),      # partial last wave, deep K: split 4 ways
+    ((2560, 2048, 2048), "pair", 1),      # partial last wave, shallow K: not worth splitting
+])
+def test_launch_plan(native_lib, shape, variant, ranges):
+    """The kernel choice (wave model) and last-wave split, computed on the host."""
+    from tensorcore_gemm import _native
+
+    assert _native.plan(*shape, sm_count=148) == (variant, ranges)
+
+
+def test_launch_plan_forced_variant_and_errors(native_lib):
+    from tensorcore_gemm import _native
+
+    _native.set_variant("pair")
+    try:
+        assert _native.plan(4096, 4096, 16384) == ("pair", 2)
+        assert _native.plan(4096, 4096, 4096)[0] == "pair"
+    finally:
+        _native.set_variant("auto")
+    _native.set_variant("skinny")
+    try:
+        assert _native.plan(4096, 4096, 4096) == ("cta1", 1)    # outside the skinny kernel's K range
+    finally:
+        _native.set_variant("auto")
+    with pytest.raises(RuntimeError):
+        _native.plan(0, 8, 8)
