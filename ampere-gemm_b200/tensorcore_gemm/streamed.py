@@ -136,3 +136,10 @@ def gemm_streamed(A_host: torch.Tensor, B: torch.Tensor, out: torch.Tensor | Non
         main.wait_stream(p.d2h)
         main.wait_stream(p.comp)
     return out
+
+
+def release_pipelines() -> None:
+    """Drop the device buffers kept for earlier gemm_streamed calls (after their
+    work has finished: synchronize first)."""
+    with _PIPELINES_LOCK:
+        _PIPELINES.clear()
