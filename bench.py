@@ -1,6 +1,6 @@
 """Benchmark of the FP16 GEMM hot path on B200 (one process per GPU).
 
-Workload: C = A @ B with M = 65536, N = K = 8192, A and B
+Workload (the reference's 1-8 GPU configuration): C = A @ B with M = 65536, N = K = 8192, A and B
 iid N(0, 0.02) fp16, A row-sharded over the N GPUs, B replicated; fp32
 accumulation, fp16 output.  One step = one pass of the GEMM over this rank's
 shard (strong scaling: total work fixed).  The inputs (A shard >= 128 MiB +
@@ -11,9 +11,13 @@ B 128 MiB per GPU) exceed the 126 MB L2, so no flush is needed between steps.
 Prints ONE JSON line on rank 0.  `value` is the whole-job TFLOP/s from CUDA
 events (max over ranks); `e2e` times the public API with the operands in
 pinned host memory (H2D of A shard + B, GEMM, D2H of C inside the timed
-region).  At N=1 rank 0 also reports the skinny K=256 shape's HBM bandwidth,
-the 8192^3 shapes in both B layouts, and torch.mm on the same box, plus the
-reference's CPU path timed on a bounded sample.
+region).  At N=1 rank 0 also reports the skinny K=256 shape's HBM bandwidth
+(against the copy rate and the read-only / write-only rates), the 8192^3
+shapes in both B layouts, torch.mm on the same box, the fused K-means
+assignment, and the reference's CPU path timed on a bounded sample.  At N>1
+it adds the gathered-output comparison (full C on every rank: GEMM + NCCL
+all-gather against the fused peer-store GEMM).  Only the result line goes to
+stdout.
 
 `--impl reference` runs the unmodified reference package (installed under
 baseline/_ref) through its public `tensorcore_gemm.gemm` on CPU tensors: its
