@@ -450,12 +450,14 @@ def gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank,
         return max_over_ranks(ev0.elapsed_time(ev1)) / steps
 
     full_nccl = torch.empty((C.shape[0] * world, C.shape[1]), dtype=C.dtype, device=dev)
+    gathered_bytes = 2 * M_TOTAL * N_DIM
 
     def separate():
         sharded.sharded_gemm(A, B, out=C)
         dist.all_gather_into_tensor(full_nccl, C)
 
     ms_sep = timed(separate)
+    ms_ag = timed(lambda: dist.all_gather_into_tensor(full_nccl, C))
     out = sharded.GatheredOutput(M_TOTAL, N_DIM, device=dev)
     try:
         ms_fused = timed(lambda: out.gemm(A, B))
@@ -466,12 +468,19 @@ def gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank,
     finally:
         out.close()
     del full_nccl
-    gathered_bytes = 2 * M_TOTAL * N_DIM
     return {"what": "C (65536 x 8192 fp16) gathered on every rank",
             "gemm_only_ms": round(gemm_ms, 4),
             "gemm_then_nccl_all_gather_ms": round(ms_sep, 4),
+            "nccl_all_gather_ms": round(ms_ag, 4),
+            "nccl_all_gather_bus_GBps": round(gathered_bytes * (world - 1) / world / (ms_ag * 1e-3) / 1e9, 1),
             "fused_peer_store_ms": round(ms_fused, 4),
             "fused_speedup": round(ms_sep / ms_fused, 3),
+            # Target of a fused compute + collective step: the slower of the GEMM
+            # and the bytes that must leave each GPU at the pool's measured
+            # 770 GB/s per direction peer-copy rate.
+            "fused_roofline_ms": round(max(gemm_ms, gathered_bytes * (world - 1) / world / 770e9 * 1e3), 4),
+            "fused_frac_of_roofline": round(max(gemm_ms, gathered_bytes * (world - 1) / world / 770e9 * 1e3)
+                                            / ms_fused, 4),
             "nvlink_bytes_out_per_gpu": int(gathered_bytes * (world - 1) // world),
             "bitwise_equal_to_nccl_path": bool(match), "steps": steps}
 
