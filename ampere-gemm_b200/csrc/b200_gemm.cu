@@ -1052,7 +1052,9 @@ extern "C" int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M
   GemmArgs g{X, Cent, nullptr, (int)M, (int)N, (int)K, ldx, ldcent, 0, EpiParams{}, dev.sm_count, stream};
   g.argmin.cnorm = cnorm;
   g.argmin.keys = keys;
-  const int rc = row_b ? launch_skinny<5, 1, true, false, true>(g) : launch_skinny<5, 1, false, false, true>(g);
+  // The argmin epilogue stages no C, so its staging space is a sixth A stage
+  // (measured ~1 % faster than five at 262144 x 1024 x 256).
+  const int rc = row_b ? launch_skinny<6, 0, true, false, true>(g) : launch_skinny<6, 0, false, false, true>(g);
   if (rc) return rc;
   unpack_keys_kernel<<<(unsigned)((M + 255) / 256), 256, 0, stream>>>(keys, (int)M, out_idx, out_score);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;

@@ -286,7 +286,8 @@ __global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
           }
           continue;
         }
-        epi_store_block<EPI_BUFS>(&tmap_c, epi_buf, epi_addr, buf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32,
+        if constexpr (!kArgmin)
+          epi_store_block<EPI_BUFS>(&tmap_c, epi_buf, epi_addr, buf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32,
                                   sc, &c_bar[ew], c_phase);
       }
       if constexpr (kArgmin) {

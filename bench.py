@@ -54,8 +54,10 @@ def parse_args():
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 side measurements")
     ap.add_argument("--case", default=None,
                     help="single-GEMM mode for profiling/tuning: MxNxK[:colb] (1 GPU, not the driver line)")
-    ap.add_argument("--variant", default="auto", choices=["auto", "cta1", "pair", "skinny", "pair2m", "torch"],
-                    help="kernel for --case (torch = torch.mm comparator)")
+    ap.add_argument("--variant", default="auto",
+                    choices=["auto", "cta1", "pair", "skinny", "pair2m", "torch", "kmeans"],
+                    help="kernel for --case (torch = torch.mm comparator; kmeans = fused K-means "
+                         "assignment of M points to N centroids, centroids stored N x K)")
     ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"], help="inputs for --case")
     ap.add_argument("--graph", action="store_true", help="--case: time a CUDA-graph replay (device time only)")
     return ap.parse_args()
@@ -649,6 +651,8 @@ def run_case(args) -> int:
     M, N, K = (int(x) for x in shape.lower().split("x"))
     colb = layout == "colb"
     dev = torch.device("cuda", 0)
+    if args.variant == "kmeans":
+        return run_kmeans_case(args, torch, M, N, K, dev)
     if args.variant != "torch":
         _native.set_variant(args.variant)
     torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
@@ -682,6 +686,27 @@ def run_case(args) -> int:
                       "TFLOPs": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
                       "GBps": round(set_bytes / (ms * 1e-3) / 1e9, 1), "operand_sets": nsets,
                       "device_error_word": err})
+    return 0 if err == 0 else 1
+
+
+def run_kmeans_case(args, torch, M, N, K, dev) -> int:
+    """`--case MxNxK --variant kmeans`: kmeans.assign of M points (M x K) to N
+    centroids (N x K) over rotating point sets (> 2x L2 together)."""
+    from tensorcore_gemm import _native, kmeans
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    point_bytes = 2 * M * K
+    nsets = max(1, min(8, -(-2 * torch.cuda.get_device_properties(dev).L2_cache_size // point_bytes)))
+    pts = [torch.randn((M, K), generator=g, device=dev, dtype=torch.float16) for _ in range(nsets)]
+    cent = torch.randn((N, K), generator=g, device=dev, dtype=torch.float16)
+    f = lambda i: kmeans.assign(pts[i % nsets], cent)
+    for i in range(max(args.warmup, 1)):
+        f(i)
+    ms = _time_launches(torch, f, args.steps)
+    err = _native.last_device_error()
+    moved = point_bytes + 2 * N * K + 4 * M
+    emit({"case": args.case, "variant": "kmeans", "us": round(ms * 1e3, 2),
+          "GBps": round(moved / (ms * 1e-3) / 1e9, 1), "point_sets": nsets, "device_error_word": err})
     return 0 if err == 0 else 1
 
 
