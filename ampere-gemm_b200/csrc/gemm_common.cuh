@@ -286,6 +286,25 @@ struct ArgminOut {
   unsigned long long* keys = nullptr;    // M entries
 };
 
+// min of three floats in one instruction (sm_100); like fminf, a NaN operand
+// yields the other operands' minimum.
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Two fmaf's in one packed instruction (fma.rn.f32x2, sm_100): d = a * b + c
+// per lane, each rounded exactly as fmaf rounds it.
+__device__ __forceinline__ void fma2f(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
 __host__ __device__ __forceinline__ uint32_t float_to_ordered(float f) {
   uint32_t u;
   memcpy(&u, &f, 4);

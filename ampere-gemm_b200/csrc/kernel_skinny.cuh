@@ -268,14 +268,22 @@ __global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
             const float4 v = nrm[q];
             const float nv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < 4; t += 2) {
               const int e = 4 * q + t;
-              d[e] = fmaf(-2.0f, __uint_as_float(e < 32 ? lo[e] : hi[e - 32]), nv[t]);
+              fma2f(d[e], d[e + 1], -2.0f, -2.0f, __uint_as_float(e < 32 ? lo[e] : hi[e - 32]),
+                    __uint_as_float(e + 1 < 32 ? lo[e + 1] : hi[e + 1 - 32]), nv[t], nv[t + 1]);
             }
           }
-          float m = d[0];
+          // Minimum by a tree of three-input mins (31 instructions, depth 4).
+          static_assert(kEpiCols == 64, "the min tree is laid out for 64 columns");
+          float t1[22], t2[8];
 #pragma unroll
-          for (int e = 1; e < kEpiCols; ++e) m = fminf(m, d[e]);
+          for (int i = 0; i < 21; ++i) t1[i] = min3f(d[3 * i], d[3 * i + 1], d[3 * i + 2]);
+          t1[21] = d[63];
+#pragma unroll
+          for (int i = 0; i < 7; ++i) t2[i] = min3f(t1[3 * i], t1[3 * i + 1], t1[3 * i + 2]);
+          t2[7] = t1[21];
+          const float m = min3f(min3f(t2[0], t2[1], t2[2]), min3f(t2[3], t2[4], t2[5]), fminf(t2[6], t2[7]));
           if (m < best_d) {
             int first = kEpiCols - 1;
 #pragma unroll
