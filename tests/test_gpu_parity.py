@@ -287,6 +287,28 @@ def test_streamed_host_operands(cuda_device, native_lib, M, N, K, chunk):
     assert torch.equal(out.cpu(), C)
 
 
+def test_streamed_back_to_back_calls_reuse_buffers(cuda_device, native_lib):
+    """Calls queued without a sync in between share the kept device buffers:
+    each call's copies and kernels must wait for the previous call's use of
+    them, whatever B, outputs and chunk counts the calls have."""
+    from tensorcore_gemm.streamed import gemm_streamed
+
+    M, N, K = 3000, 512, 768
+    runs = []
+    for i in range(3):
+        A, B = oracle.make_inputs(M, N, K, seed_a=200 + i, seed_b=300 + i)
+        runs.append((A, B, A.pin_memory(), B.pin_memory()))
+    outs = [torch.empty((M, N), dtype=torch.float16).pin_memory(),
+            torch.empty((M, N), dtype=torch.float16, device=cuda_device),
+            torch.empty((M, N), dtype=torch.float16).pin_memory()]
+    for rep in range(2):
+        for (A, B, Ah, Bh), out in zip(runs, outs):
+            gemm_streamed(Ah, Bh, out=out, chunk_rows=512)          # 6 chunks: both buffers reused
+        torch.cuda.synchronize()
+        for (A, B, Ah, Bh), out in zip(runs, outs):
+            assert_parity(out.cpu() if out.is_cuda else out, A.float() @ B.float(), K, f"back-to-back call, rep {rep}")
+
+
 PARTIAL_WAVES = [(2048, 2048, 4096), (4096, 4096, 4096), (4000, 6000, 3000), (8192, 6144, 2048), (1536, 1280, 8192)]
 
 
