@@ -77,6 +77,41 @@ def peer_shard_ptrs(peer_bases: list[int], row0: int, ldc: int, elem_bytes: int 
     return [int(b) + int(row0) * int(ldc) * elem_bytes for b in peer_bases]
 
 
+def exchange_and_open(handle: bytes, group, open_fn, close_fn, flag_device) -> list:
+    """Collective: share this rank's buffer handle, map every other rank's.
+
+    Returns the peers' mappings in rank order (own rank skipped).  Every rank
+    learns whether all of them succeeded, so a failure anywhere (an empty
+    handle: the rank could not allocate; or `open_fn` raising) makes every
+    rank close what it opened and raise together, instead of leaving some
+    rank waiting in a later collective.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    peers, failure = [], None
+    if not all(handles):
+        failure = "a rank could not allocate its IPC buffer"
+    else:
+        try:
+            for r, h in enumerate(handles):
+                if r != rank:
+                    peers.append(open_fn(h))
+        except RuntimeError as exc:
+            failure = str(exc)
+    flag = torch.tensor([1.0 if failure else 0.0], device=flag_device)
+    dist.all_reduce(flag, group=group)
+    if flag.item() > 0:
+        for p in peers:
+            close_fn(p)
+        dist.barrier(group=group)
+        raise RuntimeError(f"gathered output unavailable: {failure or 'failed on another rank'}")
+    return peers
+
+
 class _DeviceBuffer:
     """A raw device allocation exposed to torch (__cuda_array_interface__)."""
 
@@ -118,29 +153,12 @@ class GatheredOutput:
                 self._ptr, handle = _native.ipc_alloc(max(1, self.M) * self.ldc * 2)
             except RuntimeError:
                 self._ptr, handle = 0, b""
-            handles = [None] * self.world
-            dist.all_gather_object(handles, handle, group=group)
-            self._peers, failure = [], None
-            if not all(handles):
-                failure = "a rank could not allocate its IPC buffer"
-            else:
-                try:
-                    for r, h in enumerate(handles):
-                        if r != self.rank:
-                            self._peers.append(_native.ipc_open(h))
-                except RuntimeError as exc:
-                    failure = str(exc)
-            # Every rank learns whether all succeeded, so they fail together
-            # and no rank is left waiting in a later collective.
-            flag = torch.tensor([1.0 if failure else 0.0], device=self.device)
-            dist.all_reduce(flag, group=group)
-            if flag.item() > 0:
-                for p in self._peers:
-                    _native.ipc_close(p)
-                dist.barrier(group=group)
+            try:
+                self._peers = exchange_and_open(handle, group, _native.ipc_open, _native.ipc_close, self.device)
+            except RuntimeError:
                 if self._ptr:
                     _native.ipc_free(self._ptr)
-                raise RuntimeError(f"gathered output unavailable: {failure or 'failed on another rank'}")
+                raise
             self._buf = _DeviceBuffer(self._ptr, max(1, self.M), self.ldc)
             self._full = torch.as_tensor(self._buf, device=self.device)
             self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)

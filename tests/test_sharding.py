@@ -73,3 +73,62 @@ def test_peer_shard_pointers():
     ptrs = sharded.peer_shard_ptrs(bases, lo, 8192)
     assert ptrs == [b + lo * 8192 * 2 for b in bases]
     assert all(p % 16 == 0 for p in ptrs)
+
+
+def _exchange_worker(rank, world, port, scenario, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    closed = []
+    try:
+        handle = b"" if (scenario == "alloc_fails" and rank == 0) else bytes([rank + 1]) * 64
+
+        def open_fn(h):
+            if scenario == "open_fails" and rank == world - 1 and h[0] == 1:
+                raise RuntimeError("cannot map rank 0")
+            return 1000 + h[0] - 1       # "address" of the peer's buffer: 1000 + its rank
+
+        try:
+            peers = sharded.exchange_and_open(handle, None, open_fn, closed.append, "cpu")
+            q.put((rank, "ok", peers, closed))
+        except RuntimeError as exc:
+            q.put((rank, "raised", str(exc), closed))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_exchange(scenario, world=3):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, scenario, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    results = {r: rest for r, *rest in (q.get(timeout=10) for _ in procs)}
+    assert all(p.exitcode == 0 for p in procs)
+    return results
+
+
+def test_gathered_output_handshake_maps_every_peer():
+    """Each rank maps every other rank's buffer, in rank order, and closes nothing."""
+    res = _run_exchange("ok")
+    for r, (outcome, peers, closed) in res.items():
+        assert outcome == "ok"
+        assert peers == [1000 + p for p in range(3) if p != r]
+        assert closed == []
+
+
+@pytest.mark.parametrize("scenario", ["open_fails", "alloc_fails"])
+def test_gathered_output_handshake_fails_on_every_rank(scenario):
+    """One rank failing (a peer it cannot map, or no buffer of its own) makes
+    every rank raise, each after closing the mappings it had opened."""
+    res = _run_exchange(scenario)
+    for r, (outcome, detail, closed) in res.items():
+        assert outcome == "raised", (r, detail)
+        assert "gathered output unavailable" in detail
+    if scenario == "open_fails":
+        assert res[0][2] == [1001, 1002] and res[1][2] == [1000, 1002]   # opened both, closed both
+        assert res[2][2] == []                                          # failed on its first open
+    else:
+        assert all(closed == [] for _, _, closed in res.values())       # nothing was opened
