@@ -402,6 +402,21 @@ void reset_split_counters() {
       (void)cudaMemset(g_split_ws[i].counters, 0, (size_t)g_split_ws[i].max_parts * sizeof(uint32_t));
 }
 
+// Per-call launch options, set by an entry point for the duration of one
+// (host-synchronous) call on this thread.
+struct CallOptions {
+  bool no_split = false;           // run every tile whole: no split workspace (allocation-free entry)
+  uint64_t withhold_fixup_ns = 0;  // fixup-wait self-test (see SplitTail)
+  int force_variant = -1;          // >= 0: this variant instead of b200_gemm_set_variant's / auto
+};
+thread_local CallOptions t_call;
+
+struct ScopedCallOptions {
+  CallOptions saved;
+  explicit ScopedCallOptions(const CallOptions& o) : saved(t_call) { t_call = o; }
+  ~ScopedCallOptions() { t_call = saved; }
+};
+
 template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
 int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB>;
@@ -437,12 +452,15 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
   const int grid_pairs = (int)std::min<long long>(tiles, pairs);
   SplitTail st;
-  const int S = (MSUB == 1) ? split_ranges_for(tiles, grid_pairs, (K + Cfg::kStageK - 1) / Cfg::kStageK) : 1;
+  const int S = (MSUB == 1 && !t_call.no_split)
+                    ? split_ranges_for(tiles, grid_pairs, (K + Cfg::kStageK - 1) / Cfg::kStageK)
+                    : 1;
   if (S >= 2) {
     const long long r = tiles % grid_pairs;
     SplitTail s2;
     s2.dp_tiles = (int)(tiles - r);
     s2.S = S;
+    s2.withhold_fixup_ns = t_call.withhold_fixup_ns;
     if (split_workspace(stream, sm_count, s2)) st = s2;
     if (std::getenv("B200_GEMM_DEBUG"))
       std::fprintf(stderr, "b200_gemm: %lld tiles on %d pairs, last %lld tiles split %d ways%s\n", tiles, grid_pairs, r,
@@ -628,7 +646,7 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   ep.c = static_cast<uint16_t*>(C);
   ep.n_tma = n & ~7;  // a TMA store writes whole 16-byte pieces: the partial last one goes by plain stores
   const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, ep, dev.sm_count, stream};
-  int variant = g_variant;
+  int variant = t_call.force_variant >= 0 ? t_call.force_variant : g_variant;
   if (variant == B200_VARIANT_AUTO) variant = auto_variant(m, n, k, dev.sm_count);
   if (variant == B200_VARIANT_SKINNY) {
     const int rc = with_layouts(row_b, col_a, [&](auto rb, auto ca) {
@@ -904,6 +922,36 @@ extern "C" int b200_gemm_selftest_bounded_wait(int64_t limit_ns) {
   return word < 0 ? -B200_ERR_CUDA : word;
 }
 
+extern "C" int b200_gemm_selftest_split_fixup(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                              int64_t limit_ns, void* stream_ptr) {
+  using namespace b200;
+  if (limit_ns <= 0 || limit_ns > 1000000000LL) return -B200_ERR_INVALID_ARGUMENT;
+  bool done = false;
+  if (int rc = validate_args(C, M, N, K, K, N, N, B200_B_ROW_MAJOR, A, B, &done)) return -rc;
+  if (done || K == 0) return -B200_ERR_INVALID_ARGUMENT;
+  if (!pitch_ok(A, K) || !pitch_ok(B, N) || !pitch_ok(C, N)) return -B200_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int rc = current_device_info(dev)) return -rc;
+  if (!dev.sm100) return -B200_ERR_UNSUPPORTED_DEVICE;
+  const long long tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (split_ranges_for(tiles, (int)std::min<long long>(tiles, dev.sm_count / 2), (int)((K + 127) / 128)) < 2)
+    return -B200_ERR_INVALID_ARGUMENT;  // this shape's pair launch has no split last wave
+  const int before = b200_gemm_last_device_error();  // clears any earlier word
+  if (before < 0) return -B200_ERR_CUDA;
+  CallOptions opts;
+  opts.withhold_fixup_ns = static_cast<uint64_t>(limit_ns);
+  opts.force_variant = B200_VARIANT_PAIR;
+  int rc;
+  {
+    const ScopedCallOptions scoped(opts);
+    rc = gemm_aligned(A, B, C, M, N, K, K, N, N, B200_A_ROW_MAJOR, B200_B_ROW_MAJOR, EpiParams{}, dev,
+                      static_cast<cudaStream_t>(stream_ptr));
+  }
+  if (rc) return -rc;
+  const int word = b200_gemm_last_device_error();  // synchronises, clears the word, resets the tail counters
+  return word < 0 ? -B200_ERR_CUDA : word;
+}
+
 // ===========================================================================
 // Allocation-free entry point (b200_gemm_f16_noalloc)
 //
@@ -954,6 +1002,11 @@ extern "C" int b200_gemm_f16_noalloc(const void* A, const void* B, void* C, int6
   if (int rc = current_device_info(dev)) return rc;
   if (!dev.sm100) return B200_ERR_UNSUPPORTED_DEVICE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  // The split last wave of the pair kernel keeps its parts in a per-stream
+  // workspace that is allocated on first use; this entry runs every tile whole.
+  CallOptions opts;
+  opts.no_split = true;
+  const ScopedCallOptions scoped(opts);
   const RepackPlan p = plan_repack(A, B, C, M, N, K, lda, ldb, ldc, b_layout);
   if (p.bytes == 0)
     return gemm_aligned(A, B, C, M, N, K, lda, ldb, ldc, B200_A_ROW_MAJOR, b_layout, EpiParams{}, dev, stream);

@@ -334,6 +334,9 @@ struct SplitTail {
   int S = 1;                       // K ranges per tail tile (1: no split)
   float* ws = nullptr;             // parts: [tail tile][S][CTA of the pair], kPartFloats each
   uint32_t* counters = nullptr;    // [tail tile][CTA of the pair]: arrivals so far (0 between launches)
+  // Self-test of the fixup's bounded wait: when non-zero, the last unit of a
+  // tail tile issues none of its part loads and waits at most this long.
+  uint64_t withhold_fixup_ns = 0;
 };
 
 constexpr int kPartFloats = 128 * 256;  // one CTA's share of a 256 x 256 tile

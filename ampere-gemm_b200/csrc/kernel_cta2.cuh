@@ -418,7 +418,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int total = kChunks * others;
             int issued = 0;
             auto issue_upto = [&](int limit) {
-              if (lane == 0) {
+              if (lane == 0 && st.withhold_fixup_ns == 0) {
                 for (int L = issued; L < limit && L < total; ++L) {
                   const int c = L / others, i = L % others;
                   const int r = i < u.s ? i : i + 1;  // the other K ranges in order
@@ -428,9 +428,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 &fbar[L % kFixBufs]);
                 }
               }
-              issued = limit < total ? limit : total;
+              if (st.withhold_fixup_ns == 0) issued = limit < total ? limit : total;
             };
             issue_upto(kFixBufs);
+            // A fixup wait that runs out abandons the tile: C is not stored
+            // (the device error word says why), the loads still in flight
+            // into this warp's buffers are drained, and the warp still joins
+            // the epilogue barrier below.
+            bool fix_ok = true;
 #pragma unroll 1
             for (int c = 0; c < kChunks; ++c) {
               uint32_t lo[32], hi[32];
@@ -444,7 +449,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const float* src = nullptr;
                 if (r != u.s) {
                   const int L = c * others + (r < u.s ? r : r - 1);
-                  mbar_wait(&fbar[L % kFixBufs], static_cast<uint32_t>((L / kFixBufs) & 1), kDevTimeoutEpilogue);
+                  const bool arrived = __all_sync(
+                      0xffffffffu,
+                      mbar_wait(&fbar[L % kFixBufs], static_cast<uint32_t>((L / kFixBufs) & 1), kDevTimeoutSplitFixup,
+                                st.withhold_fixup_ns ? st.withhold_fixup_ns : kWaitLimitNs));
+                  if (!arrived) {
+                    if (lane == 0)
+                      for (int L2 = L; L2 < issued; ++L2)
+                        mbar_wait_drain(&fbar[L2 % kFixBufs], static_cast<uint32_t>((L2 / kFixBufs) & 1));
+                    fix_ok = false;
+                    break;
+                  }
                   src = reinterpret_cast<const float*>(fix_buf + (L % kFixBufs) * kEpiChunkF32Bytes);
                 }
 #pragma unroll
@@ -465,6 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
               }
               __syncwarp();                            // this chunk's buffers are free again
+              if (!fix_ok) break;
               issue_upto((c + 1) * others + kFixBufs);
               if (c == 0) B200_SPLIT_MARK(6, prof_s0);
 #pragma unroll

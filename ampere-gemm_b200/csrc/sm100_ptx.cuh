@@ -24,6 +24,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
   kDevTimeoutDrain = 4,      // abort path could not drain in-flight copies
   kDevTimeoutSelftest = 5,   // the self-test's deliberately unsatisfied wait ran out
+  kDevTimeoutSplitFixup = 6, // a split tile's last unit waited too long for another range's part
 };
 
 // Defined here: the library is one translation unit (csrc/b200_gemm.cu).

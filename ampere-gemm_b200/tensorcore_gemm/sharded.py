@@ -77,6 +77,23 @@ def peer_shard_ptrs(peer_bases: list[int], row0: int, ldc: int, elem_bytes: int 
     return [int(b) + int(row0) * int(ldc) * elem_bytes for b in peer_bases]
 
 
+def agree_on_failure(failure: str | None, group, flag: torch.Tensor) -> None:
+    """Collective: raise on every rank of `group` if `failure` is set on any.
+
+    `flag` is a one-element float32 tensor on the device the collective runs
+    on; it is overwritten.  On a CUDA device the all-reduce is enqueued on the
+    current stream, so it is also a device-side barrier: it completes on a rank
+    only once every rank's stream has reached it.  Reading the result back
+    synchronises this rank's current stream.
+    """
+    import torch.distributed as dist
+
+    flag.fill_(1.0 if failure else 0.0)
+    dist.all_reduce(flag, group=group)
+    if flag.item() > 0:
+        raise RuntimeError(f"gathered GEMM not run: {failure or 'failed on another rank'}")
+
+
 def exchange_and_open(handle: bytes, group, open_fn, close_fn, flag_device) -> list:
     """Collective: share this rank's buffer handle, map every other rank's.
 
@@ -173,9 +190,18 @@ class GatheredOutput:
         return row_shard_bounds(self.M, self.world, self.rank, self.align)
 
     def gemm(self, A_shard: torch.Tensor, B: torch.Tensor, b_col_major: bool = False) -> torch.Tensor:
-        """Fill `full` with [A_0; A_1; ...] @ B, A_r being rank r's rows (B as K x N, or N x K if b_col_major)."""
-        import torch.distributed as dist
+        """Fill `full` with [A_0; A_1; ...] @ B, A_r being rank r's rows (B as K x N, or N x K if b_col_major).
 
+        Collective.  Before the launch the ranks agree on their argument checks
+        with a one-element all-reduce on the current stream (a rank whose
+        operands are wrong makes every rank raise, so none is left waiting in
+        a collective); that all-reduce is also the barrier that keeps this
+        call's peer stores out of `full` until every rank's stream has passed
+        its work queued before the call.  Work that reads `full` on another
+        stream must be ordered before the next call's current stream by the
+        caller.  A second all-reduce after the launch marks every copy
+        complete; a failed launch still joins it, then raises on every rank.
+        """
         from . import _native
         from .gemm import _check_operands, _current_stream
         from .kmeans import _pitched
@@ -183,26 +209,32 @@ class GatheredOutput:
         if self._closed:
             raise RuntimeError("GatheredOutput is closed")
         lo, hi = self.bounds()
-        Bk = B.t() if b_col_major else B
-        _check_operands(A_shard, Bk)
-        if A_shard.shape[0] != hi - lo:
-            raise RuntimeError(f"rank {self.rank} shard has {A_shard.shape[0]} rows, expected {hi - lo}")
-        if Bk.shape[1] != self.N:
-            raise RuntimeError(f"B has {Bk.shape[1]} columns, the gathered output {self.N}")
-        if not b_col_major and B.stride(0) == 1 and B.stride(1) >= max(1, B.shape[0]) and B.size(0) > 1:
-            B, b_col_major = B.t(), True   # transposed view of an N x K buffer
-        A = _pitched(A_shard)
-        B = _pitched(B)
-        layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
-        K = A.shape[1]
-        c_ptr = self._ptr + lo * self.ldc * 2
+        failure = None
+        try:
+            Bk = B.t() if b_col_major else B
+            _check_operands(A_shard, Bk)
+            if A_shard.shape[0] != hi - lo:
+                raise RuntimeError(f"rank {self.rank} shard has {A_shard.shape[0]} rows, expected {hi - lo}")
+            if Bk.shape[1] != self.N:
+                raise RuntimeError(f"B has {Bk.shape[1]} columns, the gathered output {self.N}")
+            if not b_col_major and B.stride(0) == 1 and B.stride(1) >= max(1, B.shape[0]) and B.size(0) > 1:
+                B, b_col_major = B.t(), True   # transposed view of an N x K buffer
+            A = _pitched(A_shard)
+            B = _pitched(B)
+        except (RuntimeError, ValueError) as exc:
+            failure = f"rank {self.rank}: {exc}"
         with torch.cuda.device(self.device):
+            agree_on_failure(failure, self.group, self._flag)
+            layout = _native.B200_B_COL_MAJOR if b_col_major else _native.B200_B_ROW_MAJOR
+            K = A.shape[1]
+            c_ptr = self._ptr + lo * self.ldc * 2
             code = _native.gemm_gather_raw(A.data_ptr(), B.data_ptr(), c_ptr, hi - lo, self.N, K,
                                            A.stride(0), B.stride(0),
                                            self.ldc, layout, peer_shard_ptrs(self._peers, lo, self.ldc),
                                            _current_stream(self.device.index))
-            _native.check(code, "b200_gemm_f16_gather")
-            dist.all_reduce(self._flag, group=self.group)
+            launch_failure = None if code == _native.B200_OK else (
+                f"rank {self.rank}: b200_gemm_f16_gather failed: {_native.strerror(code)} (code {code})")
+            agree_on_failure(launch_failure, self.group, self._flag)
         return self.full
 
     def close(self) -> None:

@@ -165,25 +165,21 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 def load_reference_package():
     """The unmodified reference package from baseline/_ref, under its own name."""
-    import importlib.util
+    sys.path.insert(0, str(REPO))
+    from baseline import reference
 
-    init = REF_DIR / "tensorcore_gemm" / "__init__.py"
-    if not init.exists():
-        return None
-    spec = importlib.util.spec_from_file_location(
-        "_reference_tensorcore_gemm", init, submodule_search_locations=[str(init.parent)])
-    mod = importlib.util.module_from_spec(spec)
-    sys.modules[spec.name] = mod
-    spec.loader.exec_module(mod)
-    return mod
+    return reference.load_package()
 
 
 class CpuBaseline:
     """Times the reference's CPU implementation on a row slice of the workload.
 
-    kind "reference": the reference's public gemm() on CPU tensors, i.e. its
-    torch.matmul fp16 fallback (tensorcore_gemm/gemm.py:219-221), with every
-    host thread.  kind "port": the C oracle, if the reference is not installed.
+    The reference's public gemm() on CPU tensors runs its torch.matmul fp16
+    fallback (tensorcore_gemm/gemm.py:219-221).  kind "reference": that call
+    made through the unmodified package in baseline/_ref.  kind "port": the
+    package is absent, so the same torch.matmul call is made directly.  Both
+    use every host thread.  The north star's "fp16 upcast to fp32" variant,
+    torch.matmul(A.float(), B.float()), is timed beside it on the same slice.
     """
 
     def __init__(self, target_s: float = 2.0):
@@ -215,9 +211,13 @@ class CpuBaseline:
         if self.kind == "reference":
             C = self.ref.gemm(self.A, self.B, mode="reg_pingpong_256")
         else:
-            sys.path.insert(0, str(REPO))
-            from oracle import oracle
-            C, _ = oracle.gemm_f16(self.A.numpy(), self.B.numpy(), threads=self.cores, want_acc=False)
+            C = self.torch.matmul(self.A, self.B)
+        assert C.shape[0] == self.rows and C.dtype == self.torch.float16
+        return time.perf_counter() - t0
+
+    def step_fp32_upcast(self) -> float:
+        t0 = time.perf_counter()
+        C = self.torch.matmul(self.A.float(), self.B.float())
         assert C.shape[0] == self.rows
         return time.perf_counter() - t0
 
@@ -225,16 +225,19 @@ class CpuBaseline:
         return 2.0 * self.rows * N_DIM * K_DIM
 
     def sample(self) -> str:
-        path = ("reference tensorcore_gemm.gemm on CPU tensors (torch.matmul fp16 fallback)"
-                if self.kind == "reference" else "C oracle port")
+        path = ("reference tensorcore_gemm.gemm on CPU tensors (its torch.matmul fp16 fallback)"
+                if self.kind == "reference" else
+                "torch.matmul fp16 called directly (the reference's CPU call; baseline/_ref not installed)")
         return (f"{self.rows} x {N_DIM} x {K_DIM} row slice of the {M_TOTAL} x {N_DIM} x {K_DIM} workload; "
                 f"{path}; {self.cores} threads; {cpu_model()}")
 
     def measure(self, reps: int = 3) -> dict:
-        ts = sorted(self.step() for _ in range(reps))
-        t = ts[len(ts) // 2]
+        t = statistics.median(self.step() for _ in range(reps))
+        t32 = statistics.median(self.step_fp32_upcast() for _ in range(max(1, reps - 1)))
         return {"value": round(self.flops() / t / 1e12, 5), "unit": "TFLOP/s", "cores": self.cores,
-                "kind": self.kind, "sample": self.sample() + f"; median of {reps}"}
+                "kind": self.kind, "sample": self.sample() + f"; median of {reps}",
+                "fp32_upcast_value": round(self.flops() / t32 / 1e12, 5),
+                "fp32_upcast_sample": "torch.matmul(A.float(), B.float()) on the same slice and threads"}
 
 
 def run_reference(args):
@@ -255,7 +258,9 @@ def run_reference(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "f16 in / f32 accumulate (CPU torch.matmul)",
         "data": "synthetic N(0,0.02) fp16, seeded", "config": workload_config(args.gpus),
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cpu.cores, "kind": cpu.kind,
-                         "sample": cpu.sample()},
+                         "sample": cpu.sample(),
+                         "fp32_upcast_value": round(cpu.flops() / statistics.median(
+                             cpu.step_fp32_upcast() for _ in range(2)) / 1e12, 5)},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
@@ -264,6 +269,25 @@ def run_reference(args):
 
 
 BASELINE_METRIC = "FP16 GEMM TFLOPS/GPU & % dense tensor peak; HBM GB/s at K=256; box TFLOPS 1-8"
+
+
+def tensor_peak_for_clocks(peaks: dict, src: str, clk: dict) -> dict:
+    """Tensor-pipe denominator that matches the clocks seen in the timed region.
+
+    The burst GEMM figure was measured at the maximum SM clock, so a timed
+    region whose median SM clock is within 3 % of the maximum is divided by it
+    as it is.  A region that ran slower (power cap) is divided by the burst
+    figure scaled by median / maximum clock: the tensor pipe's rate is
+    proportional to the SM clock.  The sustained figure is not used; it was
+    taken at whatever clock its own loop settled to.
+    """
+    burst = float(peaks["bf16_tflops"])
+    sm, smax = clk.get("sm_mhz"), clk.get("sm_max_mhz") or peaks.get("sm_max_mhz")
+    if not sm or not smax or sm >= 0.97 * smax:
+        note = "at max clock" if sm else "clocks not sampled"
+        return {"peak": burst, "peak_source": f"{src} bf16_tflops (burst, {note}; of {src})"}
+    return {"peak": round(burst * sm / smax, 1),
+            "peak_source": f"{src} bf16_tflops (burst) x median/max SM clock {sm:.0f}/{smax:.0f} MHz"}
 
 
 def workload_config(n_gpus: int) -> dict:
@@ -385,26 +409,102 @@ def side_measurements(torch, tg, dev, peaks) -> dict:
                                "colb_frac": round(bound_us / (ms_col * 1e3), 4)},
     }
     del sets, bcol
-    # --- 8192^3, uniform inputs, both layouts; two operand sets (> L2 together)
-    n = 8192
-    ops = [((torch.rand((n, n), generator=g, device=dev) * 2 - 1).half(),
-            (torch.rand((n, n), generator=g, device=dev) * 2 - 1).half()) for _ in range(2)]
-    opsc = [b.t().contiguous() for _, b in ops]
-    Cbuf = torch.empty((n, n), device=dev, dtype=torch.float16)
-    fl = 2.0 * n ** 3
-    res = {}
-    for name, f in (("rowB", lambda i: tg.gemm(ops[i % 2][0], ops[i % 2][1], out=Cbuf)),
-                    ("colb", lambda i: tg.gemm_pretransposed(ops[i % 2][0], opsc[i % 2],
-                                                             mode="reg_pingpong_256_colb")),
-                    ("torch_mm", lambda i: torch.mm(ops[i % 2][0], ops[i % 2][1], out=Cbuf))):
-        for i in range(4):
-            f(i)
-        ms = _time_launches(torch, f, 20)
-        res[name + "_TFLOPs"] = round(fl / (ms * 1e-3) / 1e12, 1)
-    res["rowB_frac_of_measured_bf16_burst"] = round(res["rowB_TFLOPs"] / peaks["bf16_tflops"], 4)
-    out["square_8192"] = res
-    del ops, opsc, Cbuf
+    out["baseline_configs"] = config_sweep(torch, tg, dev, peaks)
     out["kmeans_assign_262144x1024x256"] = kmeans_measurement(torch, dev, g)
+    out["reference_cublas_gemm"] = reference_cublas_measurement(torch, dev)
+    return out
+
+
+# Every single-GPU configuration BASELINE names (configs 1-4): (M, N, K,
+# distribution, B layouts timed).  Config 5's one-GPU case is the main line.
+BASELINE_SHAPES = [
+    (2048, 2048, 2048, "uniform", ("rowB",)),
+    (16384, 256, 256, "normal", ("rowB", "colb")),
+    (16384, 512, 256, "normal", ("rowB", "colb")),
+    (16384, 1024, 256, "normal", ("rowB", "colb")),
+    (32768, 256, 256, "normal", ("rowB", "colb")),
+    (32768, 512, 256, "normal", ("rowB", "colb")),
+    (32768, 1024, 256, "normal", ("rowB", "colb")),
+    (4096, 4096, 4096, "uniform", ("rowB", "colb")),
+    (8192, 8192, 8192, "uniform", ("rowB", "colb")),
+    (4096, 8192, 4096, "uniform", ("rowB",)),
+    (8192, 4096, 4096, "uniform", ("rowB",)),
+    (4000, 6000, 3000, "uniform", ("rowB",)),
+]
+
+
+def config_sweep(torch, tg, dev, peaks) -> dict:
+    """Each BASELINE shape: this library (per B layout) and torch.mm (cuBLAS)
+    on the same operands, CUDA-graph replay over rotating operand sets that
+    together exceed 2x L2, so every launch reads its operands from HBM."""
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    g = torch.Generator(device=dev).manual_seed(11)
+    res = {}
+    for (M, N, K, dist, layouts) in BASELINE_SHAPES:
+        set_bytes = 2 * (M * K + K * N + M * N)
+        nsets = max(2, min(16, -(-2 * l2 // set_bytes)))
+        mk = ((lambda r, c: (torch.rand((r, c), generator=g, device=dev) * 2 - 1).half()) if dist == "uniform"
+              else (lambda r, c: torch.randn((r, c), generator=g, device=dev, dtype=torch.float16)))
+        sets = [(mk(M, K), mk(K, N), torch.empty((M, N), device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        bcol = [b.t().contiguous() for _, b, _ in sets] if "colb" in layouts else None
+        fl = 2.0 * M * N * K
+        est_us = max(fl / 1.4e15, set_bytes / 5e12) * 1e6 + 3.0
+        iters = nsets * max(1, min(400, int(30000 / est_us)) // nsets)
+        fns = {"rowB": lambda i: tg.gemm(sets[i % nsets][0], sets[i % nsets][1], out=sets[i % nsets][2]),
+               "torch_mm": lambda i: torch.mm(sets[i % nsets][0], sets[i % nsets][1], out=sets[i % nsets][2])}
+        if bcol is not None:
+            fns["colb"] = lambda i: tg.gemm(sets[i % nsets][0], bcol[i % nsets].t(), out=sets[i % nsets][2])
+        entry = {"operand_sets": nsets, "iters": iters, "dist": dist}
+        for name, f in fns.items():
+            ms = _time_graph(torch, f, iters)
+            entry[f"{name}_us"] = round(ms * 1e3, 2)
+            entry[f"{name}_TFLOPs"] = round(fl / (ms * 1e-3) / 1e12, 1)
+            if K <= 256:
+                entry[f"{name}_GBps"] = round(set_bytes / (ms * 1e-3) / 1e9, 1)
+        entry["rowB_vs_torch_mm"] = round(entry["torch_mm_us"] / entry["rowB_us"], 4)
+        if K <= 256:
+            entry["rowB_frac_of_measured_hbm"] = round(entry["rowB_GBps"] / peaks["hbm_gbs"], 4)
+        else:
+            entry["rowB_frac_of_measured_bf16_burst"] = round(entry["rowB_TFLOPs"] / peaks["bf16_tflops"], 4)
+        res[f"{M}x{N}x{K}"] = entry
+        del sets, bcol
+    torch.cuda.synchronize()
+    return res
+
+
+def reference_cublas_measurement(torch, dev) -> dict:
+    """The reference's own cuBLAS mode (tensorcore_gemm/cublas_gemm.py:29-43,
+    cublas_gemm.cu:7-62: cublasGemmEx, fp16 I/O, fp32 compute), run from the
+    unmodified package in baseline/_ref through its own JIT build
+    (cuda_compile.compile_cuda), at 8192^3 and at the main workload's shape.
+    It allocates C on every call and launches on the legacy default stream,
+    as the reference does; CUDA events on that stream, back-to-back calls."""
+    sys.path.insert(0, str(REPO))
+    from baseline import reference
+
+    try:
+        cub = reference.cublas_module()
+        if cub is None:
+            return {"unavailable": "baseline/_ref not installed"}
+        t0 = time.perf_counter()
+        cub._get_module()
+        build_s = time.perf_counter() - t0
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"reference cublas_gemm build failed: {type(exc).__name__}: {exc}"[:300]}
+    out = {"jit_build_s": round(build_s, 1),
+           "how": "reference cublas_gemm.gemm(A, B) from baseline/_ref; CUDA events over back-to-back calls"}
+    g = torch.Generator(device=dev).manual_seed(13)
+    for (M, N, K, dist, iters) in ((8192, 8192, 8192, "uniform", 20), (M_TOTAL, N_DIM, K_DIM, "normal", 10)):
+        mk = ((lambda r, c: (torch.rand((r, c), generator=g, device=dev) * 2 - 1).half()) if dist == "uniform"
+              else (lambda r, c: torch.randn((r, c), generator=g, device=dev, dtype=torch.float16) * STD))
+        ops = [(mk(M, K), mk(K, N)) for _ in range(2)]
+        f = lambda i: cub.gemm(ops[i % 2][0], ops[i % 2][1])
+        for i in range(3):
+            f(i)
+        ms = _time_launches(torch, f, iters)
+        out[f"{M}x{N}x{K}_TFLOPs"] = round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)
+        del ops
+        torch.cuda.empty_cache()
     return out
 
 
@@ -470,6 +570,8 @@ def gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank,
     finally:
         out.close()
     del full_nccl
+    link_gbs = gathered_bytes * (world - 1) / world / (ms_ag * 1e-3) / 1e9
+    roof_ms = max(gemm_ms, gathered_bytes * (world - 1) / world / (link_gbs * 1e9) * 1e3)
     return {"what": "C (65536 x 8192 fp16) gathered on every rank",
             "gemm_only_ms": round(gemm_ms, 4),
             "gemm_then_nccl_all_gather_ms": round(ms_sep, 4),
@@ -478,11 +580,12 @@ def gathered_output_measurement(torch, dist, sharded, A, B, C, dev, world, rank,
             "fused_peer_store_ms": round(ms_fused, 4),
             "fused_speedup": round(ms_sep / ms_fused, 3),
             # Target of a fused compute + collective step: the slower of the GEMM
-            # and the bytes that must leave each GPU at the pool's measured
-            # 770 GB/s per direction peer-copy rate.
-            "fused_roofline_ms": round(max(gemm_ms, gathered_bytes * (world - 1) / world / 770e9 * 1e3), 4),
-            "fused_frac_of_roofline": round(max(gemm_ms, gathered_bytes * (world - 1) / world / 770e9 * 1e3)
-                                            / ms_fused, 4),
+            # and the bytes that must leave each GPU at the link rate measured in
+            # this run (the NCCL all-gather's bus bandwidth just above).
+            "link_rate_GBps": round(link_gbs, 1),
+            "link_rate_source": "nccl_all_gather_bus_GBps of this run",
+            "fused_roofline_ms": round(roof_ms, 4),
+            "fused_frac_of_roofline": round(roof_ms / ms_fused, 4),
             "nvlink_bytes_out_per_gpu": int(gathered_bytes * (world - 1) // world),
             "bitwise_equal_to_nccl_path": bool(match), "steps": steps}
 
@@ -555,7 +658,6 @@ def run_b200(args) -> int:
     value = total_flops / (ms_max * 1e-3) / 1e12
     launch_ms = ms_local / args.steps
     achieved = 2.0 * m * N_DIM * K_DIM / (launch_ms * 1e-3) / 1e12
-    peak_key = "bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"
 
     # ---- end to end through the public API with host buffers
     e2e_steps = max(1, min(args.steps, 5))
@@ -605,6 +707,7 @@ def run_b200(args) -> int:
 
     if rank == 0:
         clk = clocks.summary()
+        rl_peak = tensor_peak_for_clocks(peaks, peaks_src, clk)
         line = {
             "metric": BASELINE_METRIC, "value": round(value, 2), "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -612,9 +715,9 @@ def run_b200(args) -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 in / f32 accumulate / f16 out",
             "data": "synthetic N(0,0.02) fp16, seeded on device", "config": workload_config(world),
             "tflops_per_gpu": round(value / world, 2),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks[peak_key],
-                         "unit": "TFLOP/s", "frac": round(achieved / peaks[peak_key], 4),
-                         "peak_source": f"{peaks_src} {peak_key}",
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
+                         **rl_peak, "frac": round(achieved / rl_peak["peak"], 4),
+                         "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
                          "traffic": read_traffic_per_launch(f"shard_{m}x{N_DIM}x{K_DIM}")},
             "pct_nominal_dense_fp16_peak": round(100 * value / world / 2250.0, 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",

@@ -93,7 +93,13 @@ B200_API int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M, 
  * implicit device synchronisation.  Operands that need re-pitching are copied
  * into a fixed 32 MiB scratch array compiled into this library (every GPU that
  * loads the library keeps it until the process exits); the call itself
- * allocates nothing.  Returns B200_ERR_SCRATCH_LIMIT when the re-pitched
+ * allocates nothing.  Every tile runs whole: the split of a partial last wave
+ * along K that b200_gemm_f16 may use (its partial sums go to a per-stream
+ * workspace allocated on first use) is never taken here, so deep-K shapes with
+ * a thin last wave can run a few percent slower than through b200_gemm_f16.
+ * The first launch of each kernel variant in a process may load that kernel's
+ * code onto the device (CUDA's lazy module loading); that is the driver's
+ * doing, not an allocation by this call.  Returns B200_ERR_SCRATCH_LIMIT when the re-pitched
  * operands (b200_gemm_workspace_size) would exceed 32 MiB; operands that need
  * no re-pitch are not limited.
  *
@@ -219,6 +225,20 @@ B200_API int b200_gemm_plan(int64_t M, int64_t N, int64_t K, int sm_count, int* 
  * the bounded wait works; the word is cleared again), or a negative
  * B200_ERR_* code.  No counterpart in the reference. */
 B200_API int b200_gemm_selftest_bounded_wait(int64_t limit_ns);
+
+/* Self-test of the split last wave's failure path: runs C = A * B (A M x K,
+ * B K x N row-major, C M x N, dense pitches) on the 256 x 256 pair kernel
+ * with its last wave split along K, but the last unit of each split tile
+ * issues none of its loads of the other K ranges' parts, so its bounded wait
+ * (`limit_ns`, 1 ns .. 1 s) runs out.  Those tiles are then left unstored
+ * (C keeps what it held there), the device error word records cause 6, and
+ * the context stays usable.  Synchronises; returns the error word it read
+ * (6 when the path works; the word and the tail counters are cleared again),
+ * or a negative B200_ERR_* code (-B200_ERR_INVALID_ARGUMENT when the shape's
+ * pair launch has no split last wave, e.g. 2560 x 2048 x 8192 does).  No
+ * counterpart in the reference. */
+B200_API int b200_gemm_selftest_split_fixup(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                            int64_t limit_ns, void* stream);
 
 /* Library ABI version (major * 100 + minor). */
 B200_API int b200_gemm_version(void);

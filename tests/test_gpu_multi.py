@@ -128,3 +128,67 @@ def test_two_rank_gathered_output(native_lib):
     res = [q.get(timeout=30) for _ in procs]
     assert all(p.exitcode == 0 for p in procs)
     assert all(ok for _, ok, _ in res), res
+
+
+def _b2b_worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for p in (str(repo), str(repo / "ampere-gemm_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensorcore_gemm import _native, sharded
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    out = None
+    try:
+        M, N, K = 4096, 2048, 1024
+        A, B1 = oracle.make_inputs(M, N, K, dist="normal", seed_a=7, seed_b=8, std=0.02)
+        _, B2 = oracle.make_inputs(M, N, K, dist="normal", seed_a=7, seed_b=9, std=0.02)
+        out = sharded.GatheredOutput(M, N, device=dev)
+        lo, hi = out.bounds()
+        Ad = A[lo:hi].to(dev)
+        oks = []
+        for _ in range(3):
+            full = out.gemm(Ad, B1.to(dev))
+            if rank == world - 1:
+                torch.cuda._sleep(100_000_000)   # a slow consumer: reads call 1's result late
+            snap = full.clone()                  # same stream as the next call
+            full2 = out.gemm(Ad, B2.to(dev))
+            torch.cuda.synchronize()
+            for got, Bx in ((snap, B1), (full2, B2)):
+                ref = A.float() @ Bx.float()
+                err = (got.float().cpu() - ref).abs().max().item()
+                oks.append(err <= 2e-3 * K ** 0.5 * ref.pow(2).mean().sqrt().item())
+        q.put((rank, all(oks) and _native.last_device_error() == 0, oks))
+    finally:
+        if out is not None:
+            out.close()
+        dist.destroy_process_group()
+
+
+def test_two_rank_gathered_output_back_to_back_with_slow_reader(native_lib):
+    """A rank's next gathered call must not store into a peer's copy while that
+    peer is still reading the previous result (the pre-launch barrier)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_b2b_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    res = [q.get(timeout=30) for _ in procs]
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(ok for _, ok, _ in res), res

@@ -100,6 +100,31 @@ def test_multi_gpu_shard_shape(cuda_device, native_lib):
     _no_device_error()
 
 
+@pytest.mark.parametrize("rows,rank", [(65536, 0), (32768, 0), (32768, 1), (16384, 3)])
+def test_bench_workload_shapes(cuda_device, native_lib, rows, rank):
+    """The bench's own launches: the 65536 x 8192 x 8192 workload on one GPU
+    (wide pair kernel, column-band raster) and its 2- and 4-rank shards, on the
+    operands bench.py generates (device generator seeded 1000 + rank for A, 1
+    for B, N(0, 0.02)), through the same call, under `auto`."""
+    N = K = 8192
+    gA = torch.Generator(device=cuda_device).manual_seed(1000 + rank)
+    gB = torch.Generator(device=cuda_device).manual_seed(1)
+    A = torch.randn((rows, K), generator=gA, device=cuda_device, dtype=torch.float16) * 0.02
+    B = torch.randn((K, N), generator=gB, device=cuda_device, dtype=torch.float16) * 0.02
+    assert _native.plan(rows, N, K)[0] == "pair2m"
+    C = torch.empty((rows, N), dtype=torch.float16, device=cuda_device)
+    tg.gemm(A, B, out=C)
+    torch.cuda.synchronize()
+    _no_device_error()
+    ref = fp32_ref(A, B)
+    assert_parity(C, ref, K, f"bench workload {rows}x{N}x{K}")
+    del ref
+    # Run to run the launch is bit-identical.
+    C2 = tg.gemm(A, B)
+    torch.cuda.synchronize()
+    assert torch.equal(C, C2)
+
+
 def test_all_modes_agree(cuda_device, variant):
     A, B = _inputs(384, 264, 320, cuda_device)
     Bc = B.t().contiguous()

@@ -63,3 +63,31 @@ def test_against_cublas(cuda_device, native_lib, M, N, K):
     lib = cublas_gemm.gemm(A, B)
     assert_parity(ours, ref, K, "b200")
     assert_parity(lib, ref, K, "cublas")
+
+
+@pytest.fixture(scope="module")
+def reference_cublas():
+    """The reference's own cuBLAS mode from the unmodified package in
+    baseline/_ref (cublas_gemm.py:29-43 over cublas_gemm.cu:7-62), built by
+    the reference's own JIT path on first use."""
+    from baseline import reference
+
+    mod = reference.cublas_module()
+    if mod is None:
+        pytest.fail("baseline/_ref is not installed: run `python baseline/install_reference.py`")
+    return mod
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 2048), (8192, 8192, 8192), (32768, 1024, 256), (4096, 8192, 4096)])
+def test_against_reference_cublas_mode(cuda_device, native_lib, reference_cublas, M, N, K):
+    A, B = oracle.make_inputs(M, N, K, dist="uniform", seed_a=5, seed_b=6)
+    A, B = A.to(cuda_device), B.to(cuda_device)
+    ref = fp32_ref(A, B)
+    ours = tg.gemm(A, B)
+    theirs = reference_cublas.gemm(A, B)
+    torch.cuda.synchronize()
+    assert_parity(ours, ref, K, "b200")
+    assert_parity(theirs, ref, K, "reference cublas_gemm")
+    bound = oracle.PARITY_COEFF * K ** 0.5 * ref.pow(2).mean().sqrt().item()
+    diff = (theirs.float() - ours.float()).abs().max().item()
+    assert diff <= 2 * bound, f"b200 vs reference cublas_gemm: {diff} > {2 * bound}"

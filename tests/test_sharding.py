@@ -132,3 +132,45 @@ def test_gathered_output_handshake_fails_on_every_rank(scenario):
         assert res[2][2] == []                                          # failed on its first open
     else:
         assert all(closed == [] for _, _, closed in res.values())       # nothing was opened
+
+
+def _agree_worker(rank, world, port, bad_rank, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        flag = torch.zeros(1)
+        failure = "shard has 100 rows, expected 128" if rank == bad_rank else None
+        try:
+            sharded.agree_on_failure(failure, None, flag)
+            outcome = "ok"
+        except RuntimeError as exc:
+            outcome = str(exc)
+        # The group is still usable afterwards: nobody was left inside a collective.
+        t = torch.tensor([float(rank)])
+        dist.all_reduce(t)
+        q.put((rank, outcome, t.item()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bad_rank", [None, 1])
+def test_gathered_gemm_agrees_on_argument_failures(bad_rank):
+    """One rank with a wrong shard makes both ranks raise before any launch
+    (GatheredOutput.gemm's pre-launch agreement); with no failure both go on."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, 2, port, bad_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    res = {r: (o, s) for r, o, s in (q.get(timeout=10) for _ in procs)}
+    assert all(p.exitcode == 0 for p in procs)
+    for r, (outcome, total) in res.items():
+        assert total == 1.0
+        if bad_rank is None:
+            assert outcome == "ok"
+        else:
+            assert "gathered GEMM not run" in outcome
+            assert ("shard has 100 rows" in outcome) == (r == bad_rank)

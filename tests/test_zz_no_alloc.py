@@ -81,3 +81,37 @@ def test_noalloc_rejects_operands_beyond_scratch(cuda_device, native_lib):
                               _native.B200_B_ROW_MAJOR, torch.cuda.current_stream().cuda_stream)
     assert rc == _native.B200_ERR_SCRATCH_LIMIT
     assert "32 MiB" in _native.strerror(rc)
+
+
+@pytest.mark.parametrize("M,N,K,ld_extra", [
+    (2560, 2048, 8192, 0),      # operands used in place; the pair kernel's last wave would split 4 ways
+    (1024, 19200, 12288, 1),    # A re-pitched into the scratch (odd lda); last wave would split 6 ways
+])
+def test_noalloc_split_shapes_allocate_nothing(cuda_device, native_lib, M, N, K, ld_extra):
+    """Shapes whose b200_gemm_f16 launch splits its last wave along K (that split
+    keeps partial sums in a per-stream workspace allocated on first use) run
+    whole through the no-alloc entry: device free memory does not move across
+    calls on a stream that has never run a GEMM."""
+    variant, ranges = _native.plan(M, N, K, torch.cuda.get_device_properties(cuda_device).multi_processor_count)
+    assert variant == "pair" and ranges > 1, (variant, ranges)
+    fn = _noalloc(native_lib)
+    A0, B0 = oracle.make_inputs(M, N, K, dist="uniform", seed_a=M, seed_b=N)
+    lda = K + ld_extra
+    Abuf = torch.zeros((M, lda), dtype=torch.float16, device=cuda_device)
+    Abuf[:, :K] = A0.to(cuda_device)
+    B = B0.to(cuda_device)
+    C = torch.empty((M, N), dtype=torch.float16, device=cuda_device)
+    args = (Abuf.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda, N, N, _native.B200_B_ROW_MAJOR)
+    # Warm-up on the current stream: the first launch of a kernel may load its code.
+    assert fn(*args, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    fresh = torch.cuda.Stream()
+    free_before = torch.cuda.mem_get_info(cuda_device)[0]
+    for _ in range(2):
+        assert fn(*args, fresh.cuda_stream) == 0
+    torch.cuda.synchronize()
+    free_after = torch.cuda.mem_get_info(cuda_device)[0]
+    assert free_after == free_before, f"device free memory moved by {free_before - free_after} bytes"
+    assert _native.last_device_error() == 0
+    A, Bd = A0.to(cuda_device), B0.to(cuda_device)
+    assert_parity(C, fp32_ref(A, Bd), K, f"no-alloc {M}x{N}x{K}")
