@@ -82,6 +82,7 @@ struct DeviceInfo {
   bool ready = false;
   bool sm100 = false;
   int sm_count = 0;
+  int64_t l2_bytes = 0;
 };
 
 std::mutex g_dev_mu;
@@ -93,12 +94,14 @@ int current_device_info(DeviceInfo& out) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DeviceInfo& d = g_dev[dev];
   if (!d.ready) {
-    int major = 0, sms = 0;
+    int major = 0, sms = 0, l2 = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) != cudaSuccess)
       return B200_ERR_CUDA;
     d.sm100 = (major == 10);
     d.sm_count = sms;
+    d.l2_bytes = l2;
     d.ready = true;
   }
   out = d;
@@ -645,6 +648,7 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   ep.ldc = ldc;
   ep.c = static_cast<uint16_t*>(C);
   ep.n_tma = n & ~7;  // a TMA store writes whole 16-byte pieces: the partial last one goes by plain stores
+  ep.c_evict_first = (dev.l2_bytes > 0 && 2 * M * N > dev.l2_bytes) ? 1 : 0;
   const GemmArgs g{A, B, C, m, n, k, lda, ldb, ldc, ep, dev.sm_count, stream};
   int variant = t_call.force_variant >= 0 ? t_call.force_variant : g_variant;
   if (variant == B200_VARIANT_AUTO) variant = auto_variant(m, n, k, dev.sm_count);

@@ -74,8 +74,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
   uint64_t* full_bar = bars;                          // [STAGES] leader: both CTAs' loads landed
   uint64_t* empty_bar = bars + STAGES;                // [STAGES] each CTA: its stage may be refilled
-  uint64_t* tmem_full = bars + 2 * STAGES;            // [kAcc]   each CTA: a tile's accumulators ready
-  uint64_t* tmem_empty = bars + 2 * STAGES + kAcc;    // [kAcc * MSUB] leader: one 256-column block drained
+  uint64_t* tmem_full = bars + 2 * STAGES;            // [kAcc * MSUB] each CTA: one 256-column block final
+  uint64_t* tmem_empty = tmem_full + kAcc * MSUB;     // [kAcc * MSUB] leader: one 256-column block drained
   uint64_t* mma_drain = tmem_empty + kAcc * MSUB;     // [1]      abort path only
   uint64_t* c_bar = mma_drain + 1;                    // [4]      old-C loads of the epilogue warps (beta != 0)
   uint64_t* fix_bar = c_bar + kEpiWarps;              // [4 x kFixBufs] split-tail fixup loads, per epilogue warp
@@ -105,7 +105,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < kAcc; ++a) mbar_init(&tmem_full[a], 1);
+    for (int a = 0; a < kAcc * MSUB; ++a) mbar_init(&tmem_full[a], 1);
     for (int a = 0; a < kAcc * MSUB; ++a) mbar_init(&tmem_empty[a], 2 * kEpiWarps);
     mbar_init(mma_drain, 1);
     for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
@@ -256,6 +256,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             issue_block(stg, u.kb0 + j, 0);
             if (++stg == STAGES) { stg = 0; ph ^= 1u; }
           }
+          if (ok && P == u.kb1 - u.kb0) {
+            // The whole tile fit these stages: block 0 is final already.
+            const uint32_t f0 = smem_u32(&tmem_full[buf * MSUB + 0]);
+            umma_commit_cta2(f0);
+            umma_commit_cta2(mapa_shared(f0, 1));
+          }
           if (ok && !B200_TIMED(1, mbar_wait_cluster(&tmem_empty[buf * MSUB + 1], acc_phase ^ 1u, kDevTimeoutMma)))
             ok = false;
           if (!ok) break;
@@ -269,7 +275,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           kb_first = u.kb0 + P;
         }
-        for (int kb = kb_first; kb < u.kb1 && ok; ++kb) {
+        // Tile end (MSUB = 2): the last P_end stages run into block 0 first,
+        // which is then published, and only then into block 1, so block 0
+        // drains while block 1's last MMAs run.
+        const int rest = u.kb1 - kb_first;
+        const int P_end = (MSUB == 2) ? (rest < STAGES ? rest : STAGES) : 0;
+        const int kb_end = u.kb1 - P_end;
+        for (int kb = kb_first; kb < kb_end && ok; ++kb) {
           if (!B200_TIMED(2, mbar_wait(&full_bar[stage], phase, kDevTimeoutMma))) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
@@ -312,7 +324,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        const uint32_t f = smem_u32(&tmem_full[buf]);
+        if constexpr (MSUB == 2) {
+          if (P_end > 0) {
+            int stg = stage;
+            uint32_t ph = phase;
+            for (int j = 0; j < P_end && ok; ++j) {
+              if (!B200_TIMED(2, mbar_wait(&full_bar[stg], ph, kDevTimeoutMma))) { ok = false; break; }
+              tc_fence_after_sync();
+              issue_block(stg, kb_end + j, 0);
+              if (++stg == STAGES) { stg = 0; ph ^= 1u; }
+            }
+            if (!ok) break;
+            const uint32_t f0 = smem_u32(&tmem_full[buf * MSUB + 0]);
+            umma_commit_cta2(f0);
+            umma_commit_cta2(mapa_shared(f0, 1));
+            for (int j = 0; j < P_end; ++j) {
+              issue_block(stage, kb_end + j, 1);
+              const uint32_t e = smem_u32(&empty_bar[stage]);
+              umma_commit_cta2(e);
+              umma_commit_cta2(mapa_shared(e, 1));
+              if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+          }
+        }
+        const uint32_t f = smem_u32(&tmem_full[buf * MSUB + MSUB - 1]);
         umma_commit_cta2(f);
         umma_commit_cta2(mapa_shared(f, 1));
       }
@@ -339,12 +374,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int buf = local % kAcc;
       const uint32_t acc_phase = (local / kAcc) & 1;
       bool got = true;
-      if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[buf], acc_phase, kDevTimeoutEpilogue));
-      got = __shfl_sync(0xffffffffu, got, 0);
-      if (!got) break;
-      tc_fence_after_sync();
 #pragma unroll 1
       for (int s = 0; s < MSUB; ++s) {
+        // Each 256-column block is published on its own barrier.
+        if (lane == 0) got = B200_TIMED(3, mbar_wait(&tmem_full[buf * MSUB + s], acc_phase, kDevTimeoutEpilogue));
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) break;
+        tc_fence_after_sync();
         const int m0 = mb * Cfg::kTileM + (static_cast<int>(rank) * MSUB + s) * kBM;
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + (buf * MSUB + s) * Cfg::kTileN;
@@ -520,6 +556,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                              &c_bar[ew], c_phase);
         }
       }
+      if (!got) break;
     }
     epi_peer_fence(sc);
     if (lane == 0) bulk_wait_group<0>();

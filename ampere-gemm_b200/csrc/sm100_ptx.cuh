@@ -136,6 +136,16 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                : "memory");
 }
 
+// The same store with an L2 cache-policy word (createpolicy) for the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const void* tmap, const void* src, int32_t x, int32_t y,
+                                                  uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+          tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "l"(cache_hint)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N committed store groups still read shared memory.

@@ -274,20 +274,25 @@ BASELINE_METRIC = "FP16 GEMM TFLOPS/GPU & % dense tensor peak; HBM GB/s at K=256
 def tensor_peak_for_clocks(peaks: dict, src: str, clk: dict) -> dict:
     """Tensor-pipe denominator that matches the clocks seen in the timed region.
 
-    The burst GEMM figure was measured at the maximum SM clock, so a timed
-    region whose median SM clock is within 3 % of the maximum is divided by it
-    as it is.  A region that ran slower (power cap) is divided by the burst
-    figure scaled by median / maximum clock: the tensor pipe's rate is
-    proportional to the SM clock.  The sustained figure is not used; it was
-    taken at whatever clock its own loop settled to.
+    The measured peaks hold two cuBLAS GEMM figures: a burst taken at the
+    maximum SM clock, and a seconds-long loop under the 1 kW power cap
+    (`bf16_tflops_sustained`, with the median clock it settled to).  A timed
+    region whose median SM clock is within 3 % of the maximum is divided by
+    the burst figure; one that ran power-capped is divided by the sustained
+    figure, measured under the same cap.  Which one was used is written in
+    `peak_source`, with the clocks.
     """
     burst = float(peaks["bf16_tflops"])
     sm, smax = clk.get("sm_mhz"), clk.get("sm_max_mhz") or peaks.get("sm_max_mhz")
-    if not sm or not smax or sm >= 0.97 * smax:
-        note = "at max clock" if sm else "clocks not sampled"
-        return {"peak": burst, "peak_source": f"{src} bf16_tflops (burst, {note}; of {src})"}
-    return {"peak": round(burst * sm / smax, 1),
-            "peak_source": f"{src} bf16_tflops (burst) x median/max SM clock {sm:.0f}/{smax:.0f} MHz"}
+    sustained = peaks.get("bf16_tflops_sustained")
+    if not sm or not smax or sm >= 0.97 * smax or not sustained:
+        note = f"timed region at {sm:.0f} of {smax:.0f} MHz" if sm and smax else "clocks not sampled"
+        return {"peak": burst, "peak_source": f"{src} bf16_tflops (burst; {note}; of {src})"}
+    settled = (peaks.get("clocks_under_load") or {}).get("sm_mhz_median")
+    return {"peak": float(sustained),
+            "peak_source": (f"{src} bf16_tflops_sustained (power-capped loop"
+                            + (f" at median {settled:.0f} MHz" if settled else "")
+                            + f"; timed region at median {sm:.0f} of {smax:.0f} MHz; of {src})")}
 
 
 def workload_config(n_gpus: int) -> dict:
