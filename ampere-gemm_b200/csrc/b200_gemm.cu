@@ -664,11 +664,12 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   }
   const int gm = group_m_override();
   if (variant == B200_VARIANT_PAIR_WIDE) {
-    // Raster: when A is much taller than B is wide, bands of 8 column blocks
-    // (65536 x 8192 x 8192, four interleaved rounds: 6320 us against 6372 for
-    // bands of 12, 6418 for 16 and 6432 for 8-row bands); otherwise bands of
-    // 8 row blocks.
-    const int group_m = gm ? gm : (m >= 4LL * n ? -8 : 8);
+    // Raster: when A is much taller than B is wide, bands of 12 column blocks
+    // (65536 x 8192 x 8192 with C stored evict-first, two interleaved rounds:
+    // 6435-6465 us against 6452-6482 for bands of 8, 6495-6579 for 16,
+    // 6689-6748 for 32 and 6561-6566 for 8-row bands; DRAM reads per launch
+    // 8.9 GB against 9.7-11.2 for bands of 8); otherwise bands of 8 row blocks.
+    const int group_m = gm ? gm : (m >= 4LL * n ? -12 : 8);
     return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
       return launch_tcgen05_pair<4, 1, 2, decltype(rb)::value, decltype(ca)::value>(g, group_m);
     });
