@@ -120,9 +120,22 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto encode = [&] {
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    // A thread that has made no runtime call yet (e.g. autograd's device
+    // thread) has no current context for this driver call: cudaSetDevice on
+    // the current device makes the primary context current, then retry.
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = encode();
+  }
+  if (r != CUDA_SUCCESS && std::getenv("B200_GEMM_DEBUG"))
+    std::fprintf(stderr, "b200_gemm: tensor map rejected (%d): base %p rows %llu cols %llu ld %llu box %u x %u\n",
+                 (int)r, base, (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)ld, box_cols,
+                 box_rows);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
@@ -420,9 +433,9 @@ struct ScopedCallOptions {
   ~ScopedCallOptions() { t_call = saved; }
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
 int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
-  using Cfg = PairConfig<STAGES, KSUB, MSUB>;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN>;
   const void *A = g.A, *B = g.B;
   void* C = g.C;
   const int M = g.M, N = g.N, K = g.K;
@@ -440,7 +453,7 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor, BN>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
@@ -521,6 +534,38 @@ int launch_skinny(const GemmArgs& g) {
 // 1.00 wide pair, 0.96 pair, 0.93 one-CTA); the model reproduces the best
 // measured variant on 2048^3 .. 8192^3, 4096 x 8192 x 4096, 8192 x 4096 x 4096,
 // 4000 x 6000 x 3000 and 65536 x 8192 x 8192.
+// Tile width of the wide pair kernel (256, 224 or 192 columns) for an
+// m x n product on `slots` resident pairs.  The MMAs of a narrower tile take
+// proportionally less time, but the kernel's stages hold the same bytes
+// whatever the width, and measured tile times barely fall with it (4000 x
+// 6000 x 3000: 120.4 us at 256 against 122.6 at 224 over the same 3 waves;
+// 4096 x 8192 x 4096: 201.6 against 198.6 over 4 waves).  So a narrower tile
+// pays only where it needs fewer waves (2560 x 2048 x 2048: 1 wave of 192-wide
+// tiles, 27.0 us, against 2 of 256-wide, 31.5 us); ties keep the widest.
+// Returns the width and, in *waves, its wave count.  B200_GEMM_WIDE_BN forces
+// one (tuning only).
+int wide_pair_bn(int m, int n, int slots, double* waves_out = nullptr) {
+  static const int forced = [] {
+    const char* e = std::getenv("B200_GEMM_WIDE_BN");
+    const int v = e ? std::atoi(e) : 0;
+    return (v == 256 || v == 224 || v == 192) ? v : 0;
+  }();
+  const int cand[3] = {256, 224, 192};
+  int best = 256;
+  long long best_w = -1;
+  for (int bn : cand) {
+    if (forced && bn != forced) continue;
+    const long long tiles = (long long)((m + 511) / 512) * ((n + bn - 1) / bn);
+    const long long w = (tiles + slots - 1) / slots;
+    if (best_w < 0 || w < best_w) {
+      best_w = w;
+      best = bn;
+    }
+  }
+  if (waves_out) *waves_out = (double)best_w;
+  return best;
+}
+
 int pick_tensor_variant(int m, int n, int k, int sm_count) {
   if (k < 512) return B200_VARIANT_CTA1;  // a pair's prologue is not amortised
   // One wave of 1-CTA tiles: every variant takes about one tile's time and the
@@ -545,6 +590,7 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
   for (const Opt& o : opts) {
     const long long tiles = (long long)((m + o.tile_m - 1) / o.tile_m) * ((n + o.tile_n - 1) / o.tile_n);
     double waves = (double)((tiles + o.slots - 1) / o.slots);
+    if (o.variant == B200_VARIANT_PAIR_WIDE) wide_pair_bn(m, n, o.slots, &waves);  // best tile width's waves
     if (o.variant == B200_VARIANT_PAIR && split_enabled() && tiles % o.slots != 0)
       waves = (double)(tiles / o.slots) + pair_tail_fraction((k + 127) / 128, tiles, o.slots);  // split last wave
     const double cost = waves * tile128_cycles * (o.rows_per_sm / 128.0) / o.rate + o.drain_cycles;
@@ -552,6 +598,11 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
       best_cost = cost;
       best = o.variant;
     }
+  }
+  if (best == B200_VARIANT_PAIR_WIDE) {
+    const int bn = wide_pair_bn(m, n, pairs);
+    if (bn == 224) return B200_VARIANT_PAIR_WIDE_224;
+    if (bn == 192) return B200_VARIANT_PAIR_WIDE_192;
   }
   return best;
 }
@@ -663,15 +714,20 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
     variant = B200_VARIANT_CTA1;  // shape outside the skinny kernel's range
   }
   const int gm = group_m_override();
-  if (variant == B200_VARIANT_PAIR_WIDE) {
+  if (variant == B200_VARIANT_PAIR_WIDE || variant == B200_VARIANT_PAIR_WIDE_224 ||
+      variant == B200_VARIANT_PAIR_WIDE_192) {
     // Raster: when A is much taller than B is wide, bands of 12 column blocks
     // (65536 x 8192 x 8192 with C stored evict-first, two interleaved rounds:
     // 6435-6465 us against 6452-6482 for bands of 8, 6495-6579 for 16,
     // 6689-6748 for 32 and 6561-6566 for 8-row bands; DRAM reads per launch
     // 8.9 GB against 9.7-11.2 for bands of 8); otherwise bands of 8 row blocks.
     const int group_m = gm ? gm : (m >= 4LL * n ? -12 : 8);
+    const int bn = variant == B200_VARIANT_PAIR_WIDE_224 ? 224 : variant == B200_VARIANT_PAIR_WIDE_192 ? 192 : 256;
     return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
-      return launch_tcgen05_pair<4, 1, 2, decltype(rb)::value, decltype(ca)::value>(g, group_m);
+      constexpr bool kRb = decltype(rb)::value, kCa = decltype(ca)::value;
+      if (bn == 224) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 224>(g, group_m);
+      if (bn == 192) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 192>(g, group_m);
+      return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 256>(g, group_m);
     });
   }
   if (variant == B200_VARIANT_PAIR) {
@@ -841,7 +897,7 @@ extern "C" int b200_gemm_f16_ws(const void* A, const void* B, void* C, int64_t M
 }
 
 extern "C" int b200_gemm_set_variant(int variant) {
-  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_PAIR_WIDE) return B200_ERR_INVALID_ARGUMENT;
+  if (variant < B200_VARIANT_AUTO || variant > B200_VARIANT_PAIR_WIDE_192) return B200_ERR_INVALID_ARGUMENT;
   b200::g_variant = variant;
   return B200_OK;
 }

@@ -146,17 +146,17 @@ struct EpiParams {
 };
 
 // Copies the 16-byte pieces of the 32 x 64 fp16 block staged at `buf`
-// (128B-swizzled, row r at r * 128) whose columns lie in [c_lo, ep.n) to
+// (128B-swizzled, row r at r * 128) whose columns lie in [c_lo, c_hi) to
 // element (x, y) of each of the `ndst` row-pitch-ldc buffers in `dst`.  Lane l
 // moves piece l % 8 of rows l / 8, l / 8 + 4, ...: one store instruction
-// writes four whole 128-byte row pieces.  A piece crossing ep.n is written
+// writes four whole 128-byte row pieces.  A piece crossing c_hi is written
 // element by element.
 __device__ __forceinline__ void epi_plain_store(const uint8_t* buf, int lane, int x, int y, const EpiParams& ep,
-                                                int c_lo, uint16_t* const* dst, int ndst) {
+                                                int c_lo, int c_hi, uint16_t* const* dst, int ndst) {
   const int seg = lane & 7;
   const int col = x + seg * 8;
-  if (col >= ep.n || col + 8 <= c_lo) return;
-  const bool whole = col + 8 <= ep.n;
+  if (col >= c_hi || col + 8 <= c_lo) return;
+  const bool whole = col + 8 <= c_hi;
 #pragma unroll 1
   for (int i = 0; i < 8; ++i) {
     const int r = i * 4 + (lane >> 3);
@@ -172,7 +172,7 @@ __device__ __forceinline__ void epi_plain_store(const uint8_t* buf, int lane, in
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int e = 0; e < 7; ++e)
-          if (e < ep.n - col) d[e] = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
+          if (e < c_hi - col) d[e] = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
       }
     }
   }
@@ -185,17 +185,22 @@ __device__ __forceinline__ void epi_plain_store(const uint8_t* buf, int lane, in
 // stores for a partial last piece and for the peers, see EpiParams).  With
 // beta != 0 the old C block is first brought into the same buffer by a TMA
 // load that completes on `cbar` (phase bit in `cphase`); the wait is bounded
-// like every other wait of the kernels.
+// like every other wait of the kernels.  `x_end` bounds the columns this
+// block may write: a tile whose width is not a multiple of 64 ends in a block
+// of which only the columns before x_end are its own; that block leaves by
+// plain stores (the next tile owns the rest of the 64).
 template <int NBUF>
 __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8_t* epi_buf, uint32_t epi_addr,
                                                 int& sbuf, int lane, const uint32_t (&lo)[32],
                                                 const uint32_t (&hi)[32], int x, int y, const EpiParams& sc,
-                                                uint64_t* cbar, uint32_t& cphase) {
+                                                uint64_t* cbar, uint32_t& cphase, int x_end = 0x7fffffff) {
   if (lane == 0) bulk_wait_group_read<NBUF - 1>();
   __syncwarp();
   uint8_t* buf = epi_buf + sbuf * kEpiBufBytes;
   const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
-  const bool tma_part = x < sc.n_tma;       // some of the block's columns go through the map
+  const bool in_tile = x + kEpiCols <= x_end;   // the whole 64-column block belongs to this tile
+  const bool load_part = x < sc.n_tma;          // old C can come in through the map (beta != 0)
+  const bool tma_part = load_part && in_tile;   // some of the block's columns leave through the map
   if (sc.alpha == 1.0f && sc.beta == 0.0f) {
     // Plain product (every call of the reference's launcher): pack the
     // accumulator bits directly; the skinny shapes are bound by this loop.
@@ -209,12 +214,12 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
     bool have_old = false;
     if (sc.beta != 0.0f) {
       bool ok = true;
-      if (lane == 0 && tma_part) {
+      if (lane == 0 && load_part) {
         mbar_arrive_expect_tx(cbar, kEpiBufBytes);
         tma_load_2d(buf, tmap_c, cbar, x, y, policy_evict_first());
         ok = mbar_wait(cbar, cphase, kDevTimeoutEpilogue);
       }
-      if (tma_part) cphase ^= 1u;
+      if (load_part) cphase ^= 1u;
       have_old = __shfl_sync(0xffffffffu, ok, 0);
     }
     const int row = y + lane;
@@ -265,8 +270,12 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
       tma_store_2d(tmap_c, buf, x, y);
     bulk_commit_group();
   }
-  if (sc.n_tma < sc.n && x + kEpiCols > sc.n_tma) epi_plain_store(buf, lane, x, y, sc, sc.n_tma, &sc.c, 1);
-  if (sc.n_peers > 0) epi_plain_store(buf, lane, x, y, sc, 0, sc.peer, sc.n_peers);
+  const int c_hi = x_end < sc.n ? x_end : sc.n;
+  if (!in_tile)
+    epi_plain_store(buf, lane, x, y, sc, x, c_hi, &sc.c, 1);
+  else if (sc.n_tma < sc.n && x + kEpiCols > sc.n_tma)
+    epi_plain_store(buf, lane, x, y, sc, sc.n_tma, sc.n, &sc.c, 1);
+  if (sc.n_peers > 0) epi_plain_store(buf, lane, x, y, sc, 0, c_hi, sc.peer, sc.n_peers);
   // The ring advances with the bulk groups: a block past the map committed
   // none, so its buffer (only read synchronously) is reused by the next block;
   // otherwise the wait above would count one group short.

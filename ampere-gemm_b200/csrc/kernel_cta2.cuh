@@ -35,12 +35,22 @@ namespace b200 {
 constexpr int kFixBufs = 6;
 constexpr uint32_t kEpiChunkF32Bytes = kEpiRows * kEpiCols * 4;  // 8 KB
 
-template <int STAGES, int KSUB, int MSUB>
+// BN: columns per pair tile (256, 224 or 192).  tcgen05.mma's time is
+// proportional to N (N / 2 cycles per 128 x N x 16 MMA for N >= 128, measured),
+// so a narrower tile costs nothing per FLOP and is picked where it fills the
+// waves better (4000 x 6000: 27 column tiles of 224 against 24 of 256).  Each
+// CTA stages 128 B columns whatever BN is and its MMAs read the first BN / 2;
+// a tile ends in a partial 64-column epilogue block when BN % 64 != 0.
+template <int STAGES, int KSUB, int MSUB, int BN = 256>
 struct PairConfig {
+  static_assert(BN == 256 || BN == 224 || BN == 192, "pair tiles are 256, 224 or 192 columns wide");
+  static_assert(BN == 256 || MSUB == 2, "narrow tiles only for the wide pair (no split tail)");
   static constexpr int kStageK = kBK * KSUB;         // K per stage (KSUB swizzle atoms)
   static constexpr int kTileM = 256 * MSUB;          // rows per pair tile
-  static constexpr int kTileN = 256;                 // columns per pair tile
-  static constexpr int kHalfN = 128;                 // B columns staged per CTA
+  static constexpr int kTileN = BN;                  // columns per pair tile
+  static constexpr int kChunksN = (BN + 63) / 64;    // 64-column epilogue blocks per 256-row block
+  static constexpr int kHalfN = 128;                 // B columns staged per CTA (>= BN / 2)
+  static constexpr int kAccCols = 256;               // TMEM columns per accumulator block (>= BN)
   static constexpr int kASub = kBM * kBK * 2;        // 16 KB: 128 rows x 64 K of A
   static constexpr int kBSub = kHalfN * kBK * 2;     // 16 KB per 64-wide K slice of B (col-major B)
   static constexpr int kABytes = kASub * KSUB * MSUB;  // A stage: [msub][ksub] blocks
@@ -51,20 +61,20 @@ struct PairConfig {
   static constexpr int kAccBufs = (MSUB == 1) ? 2 : 1;  // tiles resident in TMEM
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 512 + 1024;
-  static_assert(kAccBufs * MSUB * kTileN <= kTmemCols, "accumulators exceed TMEM");
+  static_assert(kAccBufs * MSUB * kAccCols <= kTmemCols, "accumulators exceed TMEM");
   static_assert(MSUB * KSUB * (kBK / kUmmaK) >= 8, "a pair stage needs at least 8 MMAs");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
   static_assert(MSUB != 1 || STAGES * kStageBytes >= kEpiWarps * kFixBufs * (int)kEpiChunkF32Bytes,
                 "split-tail fixup buffers must fit in the pipeline stages");
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
                                  const __grid_constant__ EpiParams sc, const __grid_constant__ SplitTail st) {
-  using Cfg = PairConfig<STAGES, KSUB, MSUB>;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN>;
   constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -141,7 +151,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int mb, nb;
         sched.tile_coords(u.t, mb, nb);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * (kBM * MSUB);
-        const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
+        const int nh0 = nb * Cfg::kTileN + static_cast<int>(rank) * (Cfg::kTileN / 2);
         for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!B200_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1u, kDevTimeoutProducer))) { ok = false; break; }
 #ifdef B200_GEMM_NOLOAD
@@ -229,7 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t adesc =
                 kAColMajor ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
                            : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
-            const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
+            const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kAccCols;
 #ifndef B200_GEMM_NOMMA
             umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
 #endif
@@ -309,7 +319,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                   kAColMajor
                       ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
                       : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
-              const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kTileN;
+              const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kAccCols;
 #ifndef B200_GEMM_NOMMA
               umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
 #endif
@@ -383,7 +393,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         const int m0 = mb * Cfg::kTileM + (static_cast<int>(rank) * MSUB + s) * kBM;
         const uint32_t t_row =
-            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + (buf * MSUB + s) * Cfg::kTileN;
+            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + (buf * MSUB + s) * Cfg::kAccCols;
 #ifdef B200_GEMM_NOEPI
         tc_fence_before_sync();
         __syncwarp();
@@ -540,20 +550,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           continue;
         }
 #pragma unroll 1
-        for (int c = 0; c < Cfg::kTileN / kEpiCols; ++c) {
+        for (int c = 0; c < Cfg::kChunksN; ++c) {
           uint32_t lo[32], hi[32];
+          // (With BN % 64 != 0 the last block's upper columns read the unused
+          // end of this accumulator block; they are never stored.)
           tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
           tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
           tmem_ld_wait_regs(lo);
           tmem_ld_wait_regs(hi);
-          if (c == Cfg::kTileN / kEpiCols - 1) {
+          if (c == Cfg::kChunksN - 1) {
             // This 256-column block is in registers: hand it back to the MMA warp.
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
           }
           epi_store_block<2>(&tmap_c, epi_buf, epi_addr, sbuf, lane, lo, hi, n0 + c * kEpiCols, m0 + quad * 32, sc,
-                             &c_bar[ew], c_phase);
+                             &c_bar[ew], c_phase, n0 + Cfg::kTileN);
         }
       }
       if (!got) break;

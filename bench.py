@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--case", default=None,
                     help="single-GEMM mode for profiling/tuning: MxNxK[:colb] (1 GPU, not the driver line)")
     ap.add_argument("--variant", default="auto",
-                    choices=["auto", "cta1", "pair", "skinny", "pair2m", "torch", "kmeans"],
+                    choices=["auto", "cta1", "pair", "skinny", "pair2m", "pair2m_224", "pair2m_192", "torch", "kmeans"],
                     help="kernel for --case (torch = torch.mm comparator; kmeans = fused K-means "
                          "assignment of M points to N centroids, centroids stored N x K)")
     ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"], help="inputs for --case")

@@ -201,6 +201,8 @@ B200_API int b200_gemm_sm_count(void);
 #define B200_VARIANT_PAIR 2 /* 2-CTA cluster (cta_group::2) kernel, 256 x 256 tiles */
 #define B200_VARIANT_SKINNY 3 /* K <= 256: B slice resident in shared memory, A streamed */
 #define B200_VARIANT_PAIR_WIDE 4 /* 2-CTA cluster kernel, 512 x 256 tiles (B reused by two MMAs) */
+#define B200_VARIANT_PAIR_WIDE_224 5 /* the same kernel with 512 x 224 tiles */
+#define B200_VARIANT_PAIR_WIDE_192 6 /* the same kernel with 512 x 192 tiles */
 
 /* Process-wide override of the kernel the library picks, for tests and
  * tuning; every variant computes the same product.  Returns

@@ -128,7 +128,10 @@ def test_gather_argument_validation_without_gpu(native_lib):
     ((2048, 2048, 2048), "cta1", 1),      # one wave of 1-CTA tiles
     ((200, 264, 136), "cta1", 1),         # K < 512
     ((2560, 2048, 8192), "pair", 4),      # partial last wave, deep K: split 4 ways
+    ((4096, 4096, 16384), "pair", 2),     # partial last wave, deep K: split 2 ways
     ((2560, 2048, 2048), "pair", 1),      # partial last wave, shallow K: not worth splitting
+    ((4000, 6000, 3000), "pair2m", 1),    # narrower wide-pair tiles would not save a wave
+    ((4096, 8192, 4096), "pair", 1),
 ])
 def test_launch_plan(native_lib, shape, variant, ranges):
     """The kernel choice (wave model) and last-wave split, computed on the host."""

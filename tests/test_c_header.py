@@ -25,8 +25,8 @@ int main(void) {
   if (b200_gemm_version() < 100) return 1;
   if (b200_gemm_plan(65536, 8192, 8192, 148, &variant, &ranges) != B200_OK) return 2;
   if (variant != B200_VARIANT_PAIR_WIDE || ranges != 1) return 3;
-  if (b200_gemm_plan(2560, 2048, 8192, 148, &variant, &ranges) != B200_OK) return 4;
-  if (variant != B200_VARIANT_PAIR || ranges != 4) return 5;
+  if (b200_gemm_plan(4096, 4096, 16384, 148, &variant, &ranges) != B200_OK) return 4;
+  if (variant != B200_VARIANT_PAIR || ranges != 2) return 5;
   /* argument checks run before any CUDA call */
   if (b200_gemm_f16(NULL, NULL, NULL, -1, 8, 8, 8, 8, 8, B200_B_ROW_MAJOR, NULL) != B200_ERR_INVALID_ARGUMENT) return 6;
   if (b200_kmeans_workspace_size(1024, 256) <= 0) return 7;

@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 GUARD = 0x7BFF  # fp16 65504: never produced by these products
 
 
-@pytest.fixture(params=["auto", "cta1", "pair", "skinny", "pair2m"])
+@pytest.fixture(params=["auto", "cta1", "pair", "skinny", "pair2m", "pair2m_224", "pair2m_192"])
 def variant(request, native_lib):
     from tensorcore_gemm import _native
 

@@ -29,7 +29,7 @@ def _inputs(M, N, K, dev, dist="uniform", seed=0, std=1.0):
     return A.to(dev), B.to(dev)
 
 
-@pytest.fixture(params=["auto", "cta1", "pair", "skinny", "pair2m"])
+@pytest.fixture(params=["auto", "cta1", "pair", "skinny", "pair2m", "pair2m_224", "pair2m_192"])
 def variant(request, native_lib):
     _native.set_variant(request.param)
     yield request.param
@@ -338,7 +338,7 @@ PARTIAL_WAVES = [(2048, 2048, 4096), (4096, 4096, 4096), (4000, 6000, 3000), (81
 
 
 @pytest.mark.parametrize("M,N,K", PARTIAL_WAVES)
-@pytest.mark.parametrize("v", ["pair", "pair2m"])
+@pytest.mark.parametrize("v", ["pair", "pair2m", "pair2m_224", "pair2m_192"])
 def test_pair_kernels_partial_last_wave(cuda_device, native_lib, M, N, K, v):
     """Pair kernels on tile counts that leave the last wave partly idle:
     within the bound, bit-identical run to run, equal in both B layouts."""
@@ -424,3 +424,27 @@ def test_column_major_a_odd_pitch_abi(cuda_device, native_lib):
     assert rc == 0
     torch.cuda.synchronize()
     assert_parity(C, fp32_ref(A, B), K)
+
+
+def test_call_from_a_fresh_host_thread(cuda_device, native_lib):
+    """A thread that has made no CUDA runtime call yet (autograd's device thread
+    is one) has no current context for the tensor-map encoder; the library
+    makes the device's primary context current and the call succeeds."""
+    import threading
+
+    A, B = _inputs(256, 320, 512, cuda_device)
+    out = {}
+
+    def work():
+        try:
+            out["C"] = tg.gemm(A, B)
+            torch.cuda.synchronize()
+        except Exception as exc:  # noqa: BLE001 - reported below
+            out["err"] = exc
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join(60)
+    assert "err" not in out, out.get("err")
+    assert_parity(out["C"], fp32_ref(A, B), 512, "fresh thread")
+    _no_device_error()
