@@ -112,8 +112,7 @@ int current_device_info(DeviceInfo& out) {
 // contiguous, `ld` elements between rows), box `box_cols` x `box_rows`,
 // 128-byte swizzle, zero fill out of bounds.
 int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
-                   uint32_t box_rows, CUtensorMapL2promotion promo,
-                   CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                   uint32_t box_rows, CUtensorMapL2promotion promo) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return B200_ERR_TENSOR_MAP;
   // A zero-extent dimension is not encodable; callers never pass one.
@@ -123,7 +122,7 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   cuuint32_t estr[2] = {1, 1};
   auto encode = [&] {
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, swz, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   };
   CUresult r = encode();
   if (r == CUDA_ERROR_INVALID_CONTEXT) {
@@ -146,10 +145,10 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 struct TmapKey {
   const void* base;
   uint64_t rows, cols, ld;
-  uint32_t box_cols, box_rows, promo, swz;
+  uint32_t box_cols, box_rows, promo;
   bool operator==(const TmapKey& o) const {
     return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box_cols == o.box_cols &&
-           box_rows == o.box_rows && promo == o.promo && swz == o.swz;
+           box_rows == o.box_rows && promo == o.promo;
   }
 };
 
@@ -162,17 +161,16 @@ struct TmapCache {
 };
 
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
-                 uint32_t box_rows, CUtensorMapL2promotion promo,
-                 CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                 uint32_t box_rows, CUtensorMapL2promotion promo) {
   static thread_local TmapCache cache;
-  const TmapKey k{base, rows, cols, ld, box_cols, box_rows, static_cast<uint32_t>(promo), static_cast<uint32_t>(swz)};
+  const TmapKey k{base, rows, cols, ld, box_cols, box_rows, static_cast<uint32_t>(promo)};
   for (int i = 0; i < TmapCache::kEntries; ++i) {
     if (cache.used[i] && cache.key[i] == k) {
       *map = cache.map[i];
       return B200_OK;
     }
   }
-  const int rc = encode_tmap_2d(map, base, rows, cols, ld, box_cols, box_rows, promo, swz);
+  const int rc = encode_tmap_2d(map, base, rows, cols, ld, box_cols, box_rows, promo);
   if (rc != B200_OK) return rc;
   const int slot = cache.next;
   cache.next = (cache.next + 1) % TmapCache::kEntries;
@@ -435,11 +433,9 @@ struct ScopedCallOptions {
   ~ScopedCallOptions() { t_call = saved; }
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256, int SK = 64>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
 int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
-  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN, SK>;
-  // K-major operand tiles: rows of SK elements, swizzled to match.
-  constexpr CUtensorMapSwizzle kKSwz = SK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN>;
   const void *A = g.A, *B = g.B;
   void* C = g.C;
   const int M = g.M, N = g.N, K = g.K;
@@ -448,16 +444,16 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   cudaStream_t stream = g.stream;
   CUtensorMap ta, tb, tc;
   int rc = kAColMajor ? make_tmap_2d(&ta, A, K, M, lda, 64, Cfg::kStageK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)
-                      : make_tmap_2d(&ta, A, M, K, lda, SK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, kKSwz);
+                      : make_tmap_2d(&ta, A, M, K, lda, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   if (kBRowMajor)
     rc = make_tmap_2d(&tb, B, K, N, ldb, 64, Cfg::kStageK, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   else
-    rc = make_tmap_2d(&tb, B, N, K, ldb, SK, Cfg::kHalfN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, kKSwz);
+    rc = make_tmap_2d(&tb, B, N, K, ldb, kBK, Cfg::kHalfN, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor, BN, SK>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor, BN>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
@@ -634,16 +630,6 @@ int group_m_override() {
   return v;
 }
 
-// K depth of a wide-pair stage row (64: 4 stages of 48 KB; 32: 8 stages of
-// 24 KB).  B200_GEMM_WIDE_SK overrides the default (tuning only).
-int wide_stage_k() {
-  static const int v = [] {
-    const char* e = std::getenv("B200_GEMM_WIDE_SK");
-    return (e && std::atoi(e) == 32) ? 32 : 64;
-  }();
-  return v;
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -739,7 +725,6 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
     const int bn = variant == B200_VARIANT_PAIR_WIDE_224 ? 224 : variant == B200_VARIANT_PAIR_WIDE_192 ? 192 : 256;
     return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
       constexpr bool kRb = decltype(rb)::value, kCa = decltype(ca)::value;
-      if (bn == 256 && wide_stage_k() == 32) return launch_tcgen05_pair<8, 1, 2, kRb, kCa, 256, 32>(g, group_m);
       if (bn == 224) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 224>(g, group_m);
       if (bn == 192) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 192>(g, group_m);
       return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 256>(g, group_m);

@@ -41,23 +41,18 @@ constexpr uint32_t kEpiChunkF32Bytes = kEpiRows * kEpiCols * 4;  // 8 KB
 // waves better (4000 x 6000: 27 column tiles of 224 against 24 of 256).  Each
 // CTA stages 128 B columns whatever BN is and its MMAs read the first BN / 2;
 // a tile ends in a partial 64-column epilogue block when BN % 64 != 0.
-template <int STAGES, int KSUB, int MSUB, int BN = 256, int SK = 64>
+template <int STAGES, int KSUB, int MSUB, int BN = 256>
 struct PairConfig {
-  // SK: K elements per row of a K-major operand tile in shared memory: 64
-  // (128-byte rows, 128-byte swizzle) or 32 (64-byte rows, 64-byte swizzle:
-  // half as many bytes per stage, twice as many stages in the same space).
-  static_assert(SK == 64 || SK == 32, "stage rows of 64 or 32 K elements");
-  static constexpr int kSK = SK;
   static_assert(BN == 256 || BN == 224 || BN == 192, "pair tiles are 256, 224 or 192 columns wide");
   static_assert(BN == 256 || MSUB == 2, "narrow tiles only for the wide pair (no split tail)");
-  static constexpr int kStageK = SK * KSUB;          // K per stage (KSUB swizzle rows)
+  static constexpr int kStageK = kBK * KSUB;         // K per stage (KSUB swizzle atoms)
   static constexpr int kTileM = 256 * MSUB;          // rows per pair tile
   static constexpr int kTileN = BN;                  // columns per pair tile
   static constexpr int kChunksN = (BN + 63) / 64;    // 64-column epilogue blocks per 256-row block
   static constexpr int kHalfN = 128;                 // B columns staged per CTA (>= BN / 2)
   static constexpr int kAccCols = 256;               // TMEM columns per accumulator block (>= BN)
-  static constexpr int kASub = kBM * SK * 2;         // 128 rows x SK of A (16 KB at SK = 64)
-  static constexpr int kBSub = kHalfN * SK * 2;      // per SK-wide K slice of B (col-major B)
+  static constexpr int kASub = kBM * kBK * 2;        // 16 KB: 128 rows x 64 K of A
+  static constexpr int kBSub = kHalfN * kBK * 2;     // 16 KB per 64-wide K slice of B (col-major B)
   static constexpr int kABytes = kASub * KSUB * MSUB;  // A stage: [msub][ksub] blocks
   static constexpr int kBBytes = kBSub * KSUB;
   static constexpr int kBPanel = kStageK * 128;      // row-major B: one 64-column panel of kStageK rows
@@ -67,28 +62,19 @@ struct PairConfig {
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiBytes + 512 + 1024;
   static_assert(kAccBufs * MSUB * kAccCols <= kTmemCols, "accumulators exceed TMEM");
-  static_assert(STAGES * MSUB * KSUB * (SK / kUmmaK) >= 16, "the ring must hold at least 16 MMAs");
+  static_assert(MSUB * KSUB * (kBK / kUmmaK) >= 8, "a pair stage needs at least 8 MMAs");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
   static_assert(MSUB != 1 || STAGES * kStageBytes >= kEpiWarps * kFixBufs * (int)kEpiChunkF32Bytes,
                 "split-tail fixup buffers must fit in the pipeline stages");
 };
 
-// Shared-memory descriptor of a K-major operand tile with SK-element rows.
-template <int SK>
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
-  if constexpr (SK == 64)
-    return make_desc_kmajor_sw128(addr);
-  else
-    return make_desc_kmajor_sw64(addr);
-}
-
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256, int SK = 64>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
                                  const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K, int group_m,
                                  const __grid_constant__ EpiParams sc, const __grid_constant__ SplitTail st) {
-  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN, SK>;
+  using Cfg = PairConfig<STAGES, KSUB, MSUB, BN>;
   constexpr int kAcc = Cfg::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -192,7 +178,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int s = 0; s < MSUB; ++s)
 #pragma unroll
               for (int sub = 0; sub < KSUB; ++sub)
-                tma_load_2d_pair(a_dst + (s * KSUB + sub) * Cfg::kASub, &tmap_a, full_leader, k0 + SK * sub,
+                tma_load_2d_pair(a_dst + (s * KSUB + sub) * Cfg::kASub, &tmap_a, full_leader, k0 + kBK * sub,
                                  m0 + kBM * s, pol_a);
           }
           if constexpr (kBRowMajor) {
@@ -203,7 +189,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll
             for (int sub = 0; sub < KSUB; ++sub)
-              tma_load_2d_pair(b_dst + sub * Cfg::kBSub, &tmap_b, full_leader, k0 + SK * sub, nh0, pol_b);
+              tma_load_2d_pair(b_dst + sub * Cfg::kBSub, &tmap_b, full_leader, k0 + kBK * sub, nh0, pol_b);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -244,15 +230,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = b_base + stg * Cfg::kBBytes;
 #pragma unroll
           for (int k = 0; k < Cfg::kStageK / kUmmaK; ++k) {
-            const int sub = k / (SK / kUmmaK), j = k % (SK / kUmmaK);
+            const int sub = k / (kBK / kUmmaK), j = k % (kBK / kUmmaK);
             uint64_t bdesc;
             if constexpr (kBRowMajor)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), Cfg::kBPanel);
             else
-              bdesc = kmajor_desc<SK>(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
+              bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
             const uint64_t adesc =
                 kAColMajor ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
-                           : kmajor_desc<SK>(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
+                           : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
             const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kAccCols;
 #ifndef B200_GEMM_NOMMA
             umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
@@ -312,12 +298,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
 #pragma unroll
           for (int k = 0; k < Cfg::kStageK / kUmmaK; ++k) {
-            const int sub = k / (SK / kUmmaK), j = k % (SK / kUmmaK);
+            const int sub = k / (kBK / kUmmaK), j = k % (kBK / kUmmaK);
             uint64_t bdesc;
             if constexpr (kBRowMajor)
               bdesc = make_desc_mnmajor_sw128(b_addr + k * (kUmmaK * 128), Cfg::kBPanel);
             else
-              bdesc = kmajor_desc<SK>(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
+              bdesc = make_desc_kmajor_sw128(b_addr + sub * Cfg::kBSub + j * (kUmmaK * 2));
 #pragma unroll
             for (int s = 0; s < MSUB; ++s) {
               if (MSUB == 1 && kb == u.kb0 && k == 0) {
@@ -332,7 +318,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               const uint64_t adesc =
                   kAColMajor
                       ? make_desc_mnmajor_sw128(a_addr + s * (Cfg::kASub * KSUB) + k * (kUmmaK * 128), Cfg::kBPanel)
-                      : kmajor_desc<SK>(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
+                      : make_desc_kmajor_sw128(a_addr + (s * KSUB + sub) * Cfg::kASub + j * (kUmmaK * 2));
               const uint32_t d_tmem = tmem_base + (buf * MSUB + s) * Cfg::kAccCols;
 #ifndef B200_GEMM_NOMMA
               umma_f16_cta2(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);

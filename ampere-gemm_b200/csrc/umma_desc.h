@@ -72,13 +72,6 @@ B200_HD uint64_t make_desc_kmajor_sw128(uint32_t smem_addr) {
   return make_smem_desc(smem_addr, 16, kSw128AtomBytes, SmemSwizzle::kSw128);
 }
 
-// K-major tile with 32 K-elements (64 bytes) per row, written by TMA with a
-// 64-byte inner box and 64-byte swizzle: row r at byte r * 64, 8-row groups of
-// 512 bytes, so SBO = 512; moving 16 K-elements is +32 bytes.
-B200_HD uint64_t make_desc_kmajor_sw64(uint32_t smem_addr) {
-  return make_smem_desc(smem_addr, 16, 512, SmemSwizzle::kSw64);
-}
-
 // MN-major tile (B row-major, K rows of N): the tile is split into panels of
 // 64 N-elements; a panel holds `k_rows` rows of 128 bytes (swizzled like
 // above) and panels follow one another every `panel_bytes`.  Then

@@ -24,7 +24,6 @@ int main() {
   std::printf("%x\n", make_idesc_f16_f32(256, 256, Major::kK, Major::kMN));
   std::printf("%x\n", make_idesc_f16_f32(128, 64, Major::kMN, Major::kK));
   std::printf("%llx\n", (unsigned long long)make_smem_desc(0x3fff0, 0x3fff0, 0x3fff0, SmemSwizzle::kNone));
-  std::printf("%llx\n", (unsigned long long)make_desc_kmajor_sw64(0x8200));
   return 0;
 }
 """
@@ -70,8 +69,3 @@ def test_instruction_descriptors(values):
 
 def test_field_masking(values):
     assert values[7] == _hand_smem(0x3FFF0, 0x3FFF0, 0x3FFF0, 0)
-
-
-def test_kmajor_sw64_descriptor(values):
-    # 64-byte rows: SBO = 8 rows x 64 B = 512, LBO unused (16), swizzle code 4.
-    assert values[8] == _hand_smem(0x8200, 16, 512, 4)
