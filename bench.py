@@ -466,10 +466,17 @@ def config_sweep(torch, tg, dev, peaks) -> dict:
         graph = est_us < 100.0
         entry = {"operand_sets": nsets, "iters": iters, "dist": dist,
                  "timing": "CUDA-graph replay" if graph else "back-to-back launches",
-                 "rounds": "best of 2 interleaved rounds"}
+                 "rounds": "best of 2 rounds in opposite orders, 0.25 s idle before each"}
         best = {}
-        for _ in range(2):
-            for name, f in fns.items():
+        names = list(fns)
+        for rnd in range(2):
+            # The order is reversed in the second round, and every measurement
+            # starts after a short idle pause, so that power-cap clock drift over
+            # the sweep does not favour whichever implementation runs first.
+            for name in (names if rnd == 0 else names[::-1]):
+                torch.cuda.synchronize()
+                time.sleep(0.25)
+                f = fns[name]
                 ms = _time_graph(torch, f, iters) if graph else _time_launches(torch, f, iters)
                 best[name] = min(best.get(name, ms), ms)
         for name, ms in best.items():
