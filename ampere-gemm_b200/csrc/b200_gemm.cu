@@ -540,8 +540,9 @@ int launch_skinny(const GemmArgs& g) {
 // whatever the width, and measured tile times barely fall with it (4000 x
 // 6000 x 3000: 120.4 us at 256 against 122.6 at 224 over the same 3 waves;
 // 4096 x 8192 x 4096: 201.6 against 198.6 over 4 waves).  So a narrower tile
-// pays only where it needs fewer waves (2560 x 2048 x 2048: 1 wave of 192-wide
-// tiles, 27.0 us, against 2 of 256-wide, 31.5 us); ties keep the widest.
+// pays only where it needs fewer waves, or within a single wave, where it
+// spreads the same work over more SMs (2560 x 2048 x 2048: 23.9-27.0 us with
+// 192-wide tiles against 31.5 with 256-wide); other ties keep the widest.
 // Returns the width and, in *waves, its wave count.  B200_GEMM_WIDE_BN forces
 // one (tuning only).
 int wide_pair_bn(int m, int n, int slots, double* waves_out = nullptr) {
@@ -557,7 +558,9 @@ int wide_pair_bn(int m, int n, int slots, double* waves_out = nullptr) {
     if (forced && bn != forced) continue;
     const long long tiles = (long long)((m + 511) / 512) * ((n + bn - 1) / bn);
     const long long w = (tiles + slots - 1) / slots;
-    if (best_w < 0 || w < best_w) {
+    // Fewest waves; among equals the widest tile, except within a single
+    // wave, where the narrowest gives each SM the least work.
+    if (best_w < 0 || w < best_w || (w == best_w && w == 1 && bn < best)) {
       best_w = w;
       best = bn;
     }
@@ -590,10 +593,17 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
   for (const Opt& o : opts) {
     const long long tiles = (long long)((m + o.tile_m - 1) / o.tile_m) * ((n + o.tile_n - 1) / o.tile_n);
     double waves = (double)((tiles + o.slots - 1) / o.slots);
-    if (o.variant == B200_VARIANT_PAIR_WIDE) wide_pair_bn(m, n, o.slots, &waves);  // best tile width's waves
+    double width = 1.0;  // tile time relative to a 256-wide tile
+    if (o.variant == B200_VARIANT_PAIR_WIDE) {
+      const int bn = wide_pair_bn(m, n, o.slots, &waves);  // best tile width's waves
+      // In a single wave of moderate depth a narrower tile does finish sooner
+      // (2560 x 2048 x 2048: 23.9 us for one wave of 192-wide tiles against
+      // 26.0 for the pair kernel's two waves); over several waves it does not.
+      if (waves <= 1.0 && k <= 4096) width = bn / 256.0;
+    }
     if (o.variant == B200_VARIANT_PAIR && split_enabled() && tiles % o.slots != 0)
       waves = (double)(tiles / o.slots) + pair_tail_fraction((k + 127) / 128, tiles, o.slots);  // split last wave
-    const double cost = waves * tile128_cycles * (o.rows_per_sm / 128.0) / o.rate + o.drain_cycles;
+    const double cost = waves * width * tile128_cycles * (o.rows_per_sm / 128.0) / o.rate + o.drain_cycles;
     if (cost < best_cost * 0.999) {
       best_cost = cost;
       best = o.variant;

@@ -129,7 +129,7 @@ def test_gather_argument_validation_without_gpu(native_lib):
     ((200, 264, 136), "cta1", 1),         # K < 512
     ((2560, 2048, 8192), "pair", 4),      # partial last wave, deep K: split 4 ways
     ((4096, 4096, 16384), "pair", 2),     # partial last wave, deep K: split 2 ways
-    ((2560, 2048, 2048), "pair", 1),      # partial last wave, shallow K: not worth splitting
+    ((2560, 2048, 2048), "pair2m_192", 1),  # one wave of 55 tiles 192 wide (256 wide: 40 tiles on 80 SMs)
     ((4000, 6000, 3000), "pair2m", 1),    # narrower wide-pair tiles would not save a wave
     ((4096, 8192, 4096), "pair", 1),
 ])
