@@ -433,7 +433,7 @@ struct ScopedCallOptions {
   ~ScopedCallOptions() { t_call = saved; }
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256, bool kDyn = false>
 int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   using Cfg = PairConfig<STAGES, KSUB, MSUB, BN>;
   const void *A = g.A, *B = g.B;
@@ -453,7 +453,7 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   if (rc) return rc;
   rc = make_tmap_2d(&tc, C, M, c_map_cols(g), ldc, kEpiCols, kEpiRows, CU_TENSOR_MAP_L2_PROMOTION_NONE);
   if (rc) return rc;
-  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor, BN>;
+  auto kern = gemm_f16_tcgen05_pair_kernel<STAGES, KSUB, MSUB, kBRowMajor, kAColMajor, BN, kDyn>;
   static std::atomic<uint8_t> attr_done[kMaxDevices];
   if (int e = ensure_smem_attr(kern, Cfg::kSmemBytes, attr_done)) return e;
   static int pairs_cache[kMaxDevices] = {0};
@@ -466,7 +466,10 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
     if (std::getenv("B200_GEMM_DEBUG")) std::fprintf(stderr, "b200_gemm: %d resident 2-CTA clusters\n", pairs);
   }
   const long long tiles = (long long)((M + Cfg::kTileM - 1) / Cfg::kTileM) * ((N + Cfg::kTileN - 1) / Cfg::kTileN);
-  const int grid_pairs = (int)std::min<long long>(tiles, pairs);
+  // Dynamic tiles launch one cluster per tile (those that have not started
+  // when a running pair needs work are cancelled and their tiles taken).
+  const int grid_pairs = kDyn ? (int)tiles : (int)std::min<long long>(tiles, pairs);
+  if (kDyn && tiles > 0x3fffffffLL) return B200_ERR_TOO_LARGE;
   SplitTail st;
   const int S = (MSUB == 1 && !t_call.no_split)
                     ? split_ranges_for(tiles, grid_pairs, (K + Cfg::kStageK - 1) / Cfg::kStageK)
@@ -640,6 +643,19 @@ int group_m_override() {
   return v;
 }
 
+// Dynamic tile scheduling of the wide pair kernel (cluster launch control),
+// used when its tiles take more than one wave: three interleaved rounds at
+// 65536 x 8192 x 8192 ran 6341-6459 us against 6461-6506 static, 4000 x 6000
+// x 3000 119.2 against 120.3; one-wave shapes have nothing to balance.
+// B200_GEMM_DYN=0 turns it off (tuning).
+bool dyn_tiles() {
+  static const bool on = [] {
+    const char* e = std::getenv("B200_GEMM_DYN");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -737,6 +753,8 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
       constexpr bool kRb = decltype(rb)::value, kCa = decltype(ca)::value;
       if (bn == 224) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 224>(g, group_m);
       if (bn == 192) return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 192>(g, group_m);
+      if (dyn_tiles() && (long long)((m + 511) / 512) * ((n + 255) / 256) > dev.sm_count / 2)
+        return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 256, true>(g, group_m);
       return launch_tcgen05_pair<4, 1, 2, kRb, kCa, 256>(g, group_m);
     });
   }

@@ -68,7 +68,14 @@ struct PairConfig {
                 "split-tail fixup buffers must fit in the pipeline stages");
 };
 
-template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256>
+// kDyn (MSUB = 2 only): the grid has one cluster per tile; a running pair
+// processes its own tile, then takes the tiles of clusters that have not
+// started yet by cancelling their launch (cluster launch control), so pairs
+// that run ahead take more tiles and the set of tiles in flight stays compact
+// in raster order.  The leader's producer fetches each next tile while the
+// current one loads and hands it to every role of both CTAs through a
+// two-slot queue in shared memory (tile -1 ends the loop).
+template <int STAGES, int KSUB, int MSUB, bool kBRowMajor, bool kAColMajor, int BN = 256, bool kDyn = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                  const __grid_constant__ CUtensorMap tmap_b,
@@ -91,6 +98,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* fix_bar = c_bar + kEpiWarps;              // [4 x kFixBufs] split-tail fixup loads, per epilogue warp
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(fix_bar + kEpiWarps * kFixBufs);
   uint32_t* split_last = tmem_base_slot + 1;          // split tail: this CTA's unit arrived last
+  static_assert(!kDyn || MSUB == 2, "dynamic tiles only for the wide pair");
+  uint8_t* bar_bytes = reinterpret_cast<uint8_t*>(bars);
+  uint8_t* clc_resp = bar_bytes + 352;                            // 16 B, dynamic tiles only
+  uint32_t* tq_tile = reinterpret_cast<uint32_t*>(bar_bytes + 368);  // [2] tile queue slots
+  uint64_t* tq_full = reinterpret_cast<uint64_t*>(bar_bytes + 384);  // [2] slot written (each CTA)
+  uint64_t* tq_empty = reinterpret_cast<uint64_t*>(bar_bytes + 400); // [2] slot read by all ten readers (leader)
+  uint64_t* clc_bar = reinterpret_cast<uint64_t*>(bar_bytes + 416);  // [1] answer of the launch-control request
+  static_assert(sizeof(uint64_t) * (2 * STAGES + 2 * kAcc * MSUB + 1 + kEpiWarps + kEpiWarps * kFixBufs) + 8 <= 352,
+                "barrier area overlaps the tile queue");
 
   B200_PROF_DECL
   const int warp = threadIdx.x >> 5;
@@ -120,6 +136,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(mma_drain, 1);
     for (int e = 0; e < kEpiWarps; ++e) mbar_init(&c_bar[e], 1);
     for (int e = 0; e < kEpiWarps * kFixBufs; ++e) mbar_init(&fix_bar[e], 1);
+    if constexpr (kDyn) {
+      for (int q = 0; q < 2; ++q) {
+        mbar_init(&tq_full[q], 1);
+        mbar_init(&tq_empty[q], 2 + 2 * kEpiWarps);  // leader MMA, peer producer, both CTAs' epilogue warps
+      }
+      mbar_init(clc_bar, 1);
+    }
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -135,6 +158,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   griddep_wait();
   griddep_launch_dependents();
 
+  // ---- dynamic tiles: the queue's reader side (any role of either CTA) ----
+  // Returns false on a timed-out wait; *tile = -1 means no more tiles.
+  auto dyn_pop = [&](int idx, int* tile, int err) -> bool {
+    const int q = idx & 1;
+    const uint32_t ph = static_cast<uint32_t>(idx >> 1) & 1u;
+    if (!mbar_wait_cluster(&tq_full[q], ph, err)) return false;
+    *tile = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(&tq_tile[q]));
+    if (leader)
+      mbar_arrive(&tq_empty[q]);
+    else
+      mbar_arrive_cluster(mapa_shared(smem_u32(&tq_empty[q]), 0));
+    return true;
+  };
+
   if (warp == 0) {
     // ---------------- TMA producer (one lane per CTA) ----------------
     if (lane == 0) {
@@ -147,7 +184,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t issued = 0;
       bool ok = true;
       WorkUnit u;
-      for (int it = 0; ok && work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it) {
+      bool clc_more = true, clc_pending = false, dyn_fail = false;
+      uint32_t clc_phase = 0;
+      // Next unit of this CTA's producer.  Dynamic tiles: the leader takes its
+      // own tile first, then the answer to the launch-control request it made
+      // when the previous tile started, publishes it to both CTAs' queues, and
+      // asks for the following one; the peer's producer reads its queue.
+      auto next_unit = [&](int it, WorkUnit& w) -> bool {
+        if constexpr (!kDyn) {
+          return work_unit(it, pair, num_pairs, num_tiles, num_kb, st, w);
+        } else {
+          int tile;
+          if (leader) {
+            if (it == 0) {
+              tile = pair;
+            } else if (clc_pending) {
+              if (!mbar_wait(clc_bar, clc_phase, kDevTimeoutProducer)) { dyn_fail = true; return false; }
+              clc_phase ^= 1u;
+              clc_pending = false;
+              uint32_t x = 0;
+              if (clc_decode(clc_resp, &x)) {
+                tile = static_cast<int>(x >> 1);
+              } else {
+                tile = -1;
+                clc_more = false;  // no request may follow a refused one
+              }
+            } else {
+              tile = -1;
+            }
+            const int q = it & 1;
+            const uint32_t ph = static_cast<uint32_t>(it >> 1) & 1u;
+            if (!mbar_wait(&tq_empty[q], ph ^ 1u, kDevTimeoutProducer)) { dyn_fail = true; return false; }
+            tq_tile[q] = static_cast<uint32_t>(tile);
+            st_shared_cluster_u32(mapa_shared(smem_u32(&tq_tile[q]), 1), static_cast<uint32_t>(tile));
+            mbar_arrive(&tq_full[q]);
+            mbar_arrive_cluster(mapa_shared(smem_u32(&tq_full[q]), 1));
+            if (tile < 0) return false;
+            if (clc_more) {
+              fence_proxy_async_smem();  // the previous answer was read before the next one is written
+              mbar_arrive_expect_tx(clc_bar, 16);
+              clc_try_cancel(clc_resp, clc_bar);
+              clc_pending = true;
+            }
+          } else {
+            if (!dyn_pop(it, &tile, kDevTimeoutProducer)) { dyn_fail = true; return false; }
+            if (tile < 0) return false;
+          }
+          w.t = tile;
+          w.kb0 = 0;
+          w.kb1 = num_kb;
+          w.s = -1;
+          return true;
+        }
+      };
+      for (int it = 0; ok && next_unit(it, u); ++it) {
         int mb, nb;
         sched.tile_coords(u.t, mb, nb);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(rank) * (kBM * MSUB);
@@ -195,6 +285,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      if (dyn_fail) ok = false;
+      if (clc_pending) mbar_wait_drain(clc_bar, clc_phase);  // no request may be in flight at exit
       if (!ok && leader) {
         const uint32_t pending = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
         int s = stage;
@@ -221,7 +313,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const long long prof_t0 = clock64();
 #endif
       WorkUnit u;
-      for (int it = 0; ok && work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it, ++local) {
+      auto next_unit = [&](int it, WorkUnit& w) -> bool {
+        if constexpr (!kDyn) {
+          return work_unit(it, pair, num_pairs, num_tiles, num_kb, st, w);
+        } else {
+          int tile = -1;
+          if (!dyn_pop(it, &tile, kDevTimeoutMma)) { ok = false; return false; }
+          if (tile < 0) return false;
+          w.t = tile;
+          w.kb0 = 0;
+          w.kb1 = num_kb;
+          w.s = -1;
+          return true;
+        }
+      };
+      for (int it = 0; ok && next_unit(it, u); ++it, ++local) {
         const int buf = local % kAcc;
         const uint32_t acc_phase = (local / kAcc) & 1;
         // The MMAs of one K step: 256-column block s of this tile's accumulator.
@@ -377,7 +483,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t c_phase = 0;
     int local = 0;
     WorkUnit u;
-    for (int it = 0; work_unit(it, pair, num_pairs, num_tiles, num_kb, st, u); ++it, ++local) {
+    auto next_unit = [&](int it, WorkUnit& w) -> bool {
+      if constexpr (!kDyn) {
+        return work_unit(it, pair, num_pairs, num_tiles, num_kb, st, w);
+      } else {
+        int tile = -1;
+        bool popped = true;
+        if (lane == 0) popped = dyn_pop(it, &tile, kDevTimeoutEpilogue);
+        popped = __shfl_sync(0xffffffffu, popped, 0);
+        tile = __shfl_sync(0xffffffffu, tile, 0);
+        if (!popped || tile < 0) return false;
+        w.t = tile;
+        w.kb0 = 0;
+        w.kb1 = num_kb;
+        w.s = -1;
+        return true;
+      }
+    };
+    for (int it = 0; next_unit(it, u); ++it, ++local) {
       int mb, nb;
       sched.tile_coords(u.t, mb, nb);
       const int n0 = nb * Cfg::kTileN;

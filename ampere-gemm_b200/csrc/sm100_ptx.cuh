@@ -344,6 +344,38 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Cluster launch control: ask the hardware to cancel the launch of a cluster
+// of this grid that has not started yet; the 16-byte answer lands in this
+// CTA's shared memory at `resp` and completes as transaction bytes on `bar`
+// (no multicast form: only the calling CTA receives it).
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+                   smem_u32(resp)),
+               "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Decodes an answer of clc_try_cancel: true and the first CTA index (x) of the
+// cancelled cluster, or false when no cluster was left to cancel.
+__device__ __forceinline__ bool clc_decode(const void* resp, uint32_t* first_ctaid_x) {
+  uint32_t ok = 0, x = 0;
+  asm volatile(
+      "{\n\t.reg .b128 q;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 q, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, q;\n\t}"
+      : "=r"(ok), "=r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  *first_ctaid_x = x;
+  return ok != 0;
+}
+
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 // Full cluster barrier (all threads of all CTAs of the cluster).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -448,3 +448,41 @@ def test_call_from_a_fresh_host_thread(cuda_device, native_lib):
     assert "err" not in out, out.get("err")
     assert_parity(out["C"], fp32_ref(A, B), 512, "fresh thread")
     _no_device_error()
+
+
+_DYN_CHILD = r"""
+import sys
+sys.path[:0] = [sys.argv[1], sys.argv[1] + '/ampere-gemm_b200']
+import torch, tensorcore_gemm as tg
+from tensorcore_gemm import _native
+g = torch.Generator(device='cuda').manual_seed(9)
+A = (torch.randn((8192, 2048), generator=g, device='cuda') * 0.05).half()
+B = (torch.randn((2048, 4096), generator=g, device='cuda') * 0.05).half()
+_native.set_variant('pair2m')
+C = tg.gemm(A, B)
+torch.cuda.synchronize()
+assert _native.last_device_error() == 0
+torch.save(C.cpu(), sys.argv[2])
+"""
+
+
+def test_dynamic_and_static_tile_order_agree(cuda_device, native_lib, tmp_path):
+    """The wide pair kernel's dynamic tile scheduling (cluster launch control,
+    the default for multi-wave launches) and its static round-robin order give
+    bit-identical results: each tile is computed once, the same way."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = str(Path(__file__).resolve().parent.parent)
+    outs = {}
+    for dyn in ("1", "0"):
+        out = tmp_path / f"c{dyn}.pt"
+        env = dict(os.environ, B200_GEMM_DYN=dyn)
+        r = subprocess.run([sys.executable, "-c", _DYN_CHILD, repo, str(out)], env=env, capture_output=True,
+                           text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs[dyn] = torch.load(out)
+    assert torch.equal(outs["1"], outs["0"])
+
