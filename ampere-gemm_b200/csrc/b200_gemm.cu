@@ -471,7 +471,7 @@ int launch_tcgen05_pair(const GemmArgs& g, int group_m) {
   const int grid_pairs = kDyn ? (int)tiles : (int)std::min<long long>(tiles, pairs);
   if (kDyn && tiles > 0x3fffffffLL) return B200_ERR_TOO_LARGE;
   SplitTail st;
-  const int S = (MSUB == 1 && !t_call.no_split)
+  const int S = (MSUB == 1 && !kDyn && !t_call.no_split)
                     ? split_ranges_for(tiles, grid_pairs, (K + Cfg::kStageK - 1) / Cfg::kStageK)
                     : 1;
   if (S >= 2) {
@@ -760,8 +760,15 @@ int gemm_aligned(const void* A, const void* B, void* C, int64_t M, int64_t N, in
   }
   if (variant == B200_VARIANT_PAIR) {
     const int group_m = gm ? gm : 8;  // 8 x 256-row bands: fewest DRAM bytes measured at 8192^3
+    // Several waves and no split last wave: dynamic tiles, as for the wide pair.
+    const long long tiles = (long long)((m + 255) / 256) * ((n + 255) / 256);
+    const int pairs = dev.sm_count / 2;
+    const bool dyn = dyn_tiles() && tiles > pairs &&
+                     (t_call.no_split || split_ranges_for(tiles, pairs, (k + 127) / 128) == 1);
     return with_layouts(row_b, col_a, [&](auto rb, auto ca) {
-      return launch_tcgen05_pair<3, 2, 1, decltype(rb)::value, decltype(ca)::value>(g, group_m);
+      constexpr bool kRb = decltype(rb)::value, kCa = decltype(ca)::value;
+      if (dyn) return launch_tcgen05_pair<3, 2, 1, kRb, kCa, 256, true>(g, group_m);
+      return launch_tcgen05_pair<3, 2, 1, kRb, kCa, 256>(g, group_m);
     });
   }
   const int group_m = gm ? gm : 16;  // 16 x 128-row bands: fewest DRAM bytes measured at 8192^3

@@ -68,7 +68,7 @@ struct PairConfig {
                 "split-tail fixup buffers must fit in the pipeline stages");
 };
 
-// kDyn (MSUB = 2 only): the grid has one cluster per tile; a running pair
+// kDyn (no split tail): the grid has one cluster per tile; a running pair
 // processes its own tile, then takes the tiles of clusters that have not
 // started yet by cancelling their launch (cluster launch control), so pairs
 // that run ahead take more tiles and the set of tiles in flight stays compact
@@ -98,7 +98,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* fix_bar = c_bar + kEpiWarps;              // [4 x kFixBufs] split-tail fixup loads, per epilogue warp
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(fix_bar + kEpiWarps * kFixBufs);
   uint32_t* split_last = tmem_base_slot + 1;          // split tail: this CTA's unit arrived last
-  static_assert(!kDyn || MSUB == 2, "dynamic tiles only for the wide pair");
   uint8_t* bar_bytes = reinterpret_cast<uint8_t*>(bars);
   uint8_t* clc_resp = bar_bytes + 352;                            // 16 B, dynamic tiles only
   uint32_t* tq_tile = reinterpret_cast<uint32_t*>(bar_bytes + 368);  // [2] tile queue slots
