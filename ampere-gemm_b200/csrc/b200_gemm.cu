@@ -525,7 +525,7 @@ int launch_skinny(const GemmArgs& g) {
   const long long tiles = (long long)((M + kBM - 1) / kBM) * num_nb;
   const int slots = (sm_count / num_nb) * num_nb;
   const int grid = (int)std::min<long long>(tiles, slots);
-  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3((kArgmin || EPI_W == 8) ? 320 : kThreads), Cfg::kSmemBytes, stream, ta, tb,
+  const cudaError_t le = launch_gemm(kern, dim3(grid), dim3(skinny_threads(kArgmin, EPI_W)), Cfg::kSmemBytes, stream, ta, tb,
                                      tc, M, N, K, g.scale, g.argmin);
   return le == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
@@ -1203,7 +1203,11 @@ extern "C" int b200_kmeans_assign_f16(const void* X, const void* Cent, int64_t M
   g.argmin.keys = keys;
   // The argmin epilogue stages no C, so its staging space is a sixth A stage
   // (measured ~1 % faster than five at 262144 x 1024 x 256).
-  const int rc = row_b ? launch_skinny<6, 0, true, false, true>(g) : launch_skinny<6, 0, false, false, true>(g);
+  // 16 epilogue warps for K <= 128, 8 above (B200_GEMM_KM16=0/1 forces one; tuning only).
+  static const int km16_env = [] { const char* e = std::getenv("B200_GEMM_KM16"); return e ? std::atoi(e) : -1; }();
+  const bool km16 = km16_env >= 0 ? km16_env == 1 : K <= 128;
+  const int rc = km16 ? (row_b ? launch_skinny<6, 0, true, false, true, 16>(g) : launch_skinny<6, 0, false, false, true, 16>(g))
+                      : (row_b ? launch_skinny<6, 0, true, false, true>(g) : launch_skinny<6, 0, false, false, true>(g));
   if (rc) return rc;
   unpack_keys_kernel<<<(unsigned)((M + 255) / 256), 256, 0, stream>>>(keys, (int)M, out_idx, out_score);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;

@@ -36,8 +36,14 @@ struct SkinnyConfig {
   static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeds 227 KB");
 };
 
+// Threads of a skinny launch: two role warps plus the epilogue warps (argmin
+// mode: 8, or 16 when EPI_W is 16).
+constexpr int skinny_threads(bool argmin, int epi_w) {
+  return argmin ? (epi_w == 16 ? 64 + 16 * 32 : 320) : (epi_w == 8 ? 320 : kThreads);
+}
+
 template <int A_STAGES, int EPI_BUFS, bool kBRowMajor, bool kAColMajor, bool kArgmin = false, int EPI_W = kEpiWarps>
-__global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
+__global__ void __launch_bounds__(skinny_threads(kArgmin, EPI_W), 1)
     gemm_f16_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_c, int M, int N, int K,
                            const __grid_constant__ EpiParams sc, const ArgminOut am = ArgminOut{}) {
@@ -45,9 +51,12 @@ __global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
   // The epilogue sets the pace of this kernel (per tile it drains 128 x 256
   // fp32 while the MMAs take ~2k cycles), so it may run on 8 warps: two per
   // TMEM lane quadrant, each on half of the columns.  The argmin epilogue
-  // always does.
-  constexpr int kEpiW = kArgmin ? 8 : EPI_W;
-  static_assert(EPI_W == 4 || EPI_W == 8, "4 or 8 epilogue warps");
+  // runs on 8 warps, or on 16 (four per quadrant, one 64-column chunk each,
+  // scored per 32-column half to stay within 112 registers) when its caller
+  // asks: measured faster for K <= 128 (65536 x 4096 x 128: 93.5 against
+  // 115.0 us), slower for K = 256 (262144 x 1024 x 256: 132.6 against 124.9).
+  constexpr int kEpiW = kArgmin ? (EPI_W == 16 ? 16 : 8) : EPI_W;
+  static_assert(EPI_W == 4 || EPI_W == 8 || (kArgmin && EPI_W == 16), "4 or 8 epilogue warps (16: argmin only)");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_b = smem;                                   // resident B slice
@@ -89,7 +98,7 @@ __global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
     }
     for (int kb = 0; kb < Cfg::kMaxKBlocks; ++kb) mbar_init(&b_full[kb], 1);
     mbar_init(mma_drain, 1);
-    for (int e = 0; e < kEpiW; ++e) mbar_init(&c_bar[e], 1);
+    for (int e = 0; e < (kEpiW < 8 ? kEpiW : 8); ++e) mbar_init(&c_bar[e], 1);  // [8] slots; argmin uses none
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -244,6 +253,50 @@ __global__ void __launch_bounds__((kArgmin || EPI_W == 8) ? 320 : kThreads, 1)
       int best_i = 0x7fffffff;
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
+        if constexpr (kArgmin && kEpiW == 16) {
+          // Per 32-column half: its scores, their minimum (a tree of
+          // three-input mins), then the first column reaching it; a later
+          // half or chunk replaces the best only when strictly smaller, so
+          // ties go to the smallest index.
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32 * h, r);
+            tmem_ld_wait_regs(r);
+            if (h == 1 && c == c_end - 1) {
+              tc_fence_before_sync();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            }
+            float d[32];
+            const float4* nrm = reinterpret_cast<const float4*>(s_norm + c * kEpiCols + 32 * h);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 v = nrm[q];
+              fma2f(d[4 * q], d[4 * q + 1], -2.0f, -2.0f, __uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                    v.x, v.y);
+              fma2f(d[4 * q + 2], d[4 * q + 3], -2.0f, -2.0f, __uint_as_float(r[4 * q + 2]),
+                    __uint_as_float(r[4 * q + 3]), v.z, v.w);
+            }
+            float t1[11], t2[4];
+#pragma unroll
+            for (int i = 0; i < 10; ++i) t1[i] = min3f(d[3 * i], d[3 * i + 1], d[3 * i + 2]);
+            t1[10] = fminf(d[30], d[31]);
+#pragma unroll
+            for (int i = 0; i < 3; ++i) t2[i] = min3f(t1[3 * i], t1[3 * i + 1], t1[3 * i + 2]);
+            t2[3] = fminf(t1[9], t1[10]);
+            const float m = fminf(min3f(t2[0], t2[1], t2[2]), t2[3]);
+            if (m < best_d) {
+              int first = 31;
+#pragma unroll
+              for (int e = 31; e >= 0; --e)
+                if (d[e] == m) first = e;
+              best_d = m;
+              best_i = n0 + c * kEpiCols + 32 * h + first;
+            }
+          }
+          continue;
+        }
         uint32_t lo[32], hi[32];
 #ifdef B200_GEMM_PROFILE
         const long long prof_l0 = clock64();
