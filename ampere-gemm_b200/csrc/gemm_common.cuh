@@ -178,6 +178,36 @@ __device__ __forceinline__ void epi_plain_store(const uint8_t* buf, int lane, in
   }
 }
 
+// Second half of an epilogue block store: the staged 32 x 64 fp16 block at
+// `buf` leaves through the TMA map (columns before n_tma, whole blocks of this
+// tile), by plain stores (columns past the map or past x_end), and to the
+// peers' copies in gathered-output mode; the staging ring then advances.
+template <int NBUF>
+__device__ __forceinline__ void epi_issue_store(const CUtensorMap* tmap_c, uint8_t* buf, int& sbuf, int lane, int x,
+                                                int y, const EpiParams& sc, int x_end) {
+  const bool in_tile = x + kEpiCols <= x_end;
+  const bool tma_part = x < sc.n_tma && in_tile;
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && tma_part) {
+    if (sc.c_evict_first)
+      tma_store_2d_hint(tmap_c, buf, x, y, policy_evict_first());
+    else
+      tma_store_2d(tmap_c, buf, x, y);
+    bulk_commit_group();
+  }
+  const int c_hi = x_end < sc.n ? x_end : sc.n;
+  if (!in_tile)
+    epi_plain_store(buf, lane, x, y, sc, x, c_hi, &sc.c, 1);
+  else if (sc.n_tma < sc.n && x + kEpiCols > sc.n_tma)
+    epi_plain_store(buf, lane, x, y, sc, sc.n_tma, sc.n, &sc.c, 1);
+  if (sc.n_peers > 0) epi_plain_store(buf, lane, x, y, sc, 0, c_hi, sc.peer, sc.n_peers);
+  // The ring advances with the bulk groups: a block past the map committed
+  // none, so its buffer (only read synchronously) is reused by the next block;
+  // otherwise the wait above would count one group short.
+  if (tma_part) sbuf = (sbuf + 1) % NBUF;
+}
+
 // Writes one 32-row x 64-column block of C from the calling warp: lane l holds
 // row l's 64 fp32 values in lo (columns 0..31) and hi (32..63).  The block goes
 // through the warp's 128B-swizzled staging buffer (`NBUF` buffers, `sbuf`
@@ -198,9 +228,7 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
   __syncwarp();
   uint8_t* buf = epi_buf + sbuf * kEpiBufBytes;
   const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
-  const bool in_tile = x + kEpiCols <= x_end;   // the whole 64-column block belongs to this tile
   const bool load_part = x < sc.n_tma;          // old C can come in through the map (beta != 0)
-  const bool tma_part = load_part && in_tile;   // some of the block's columns leave through the map
   if (sc.alpha == 1.0f && sc.beta == 0.0f) {
     // Plain product (every call of the reference's launcher): pack the
     // accumulator bits directly; the skinny shapes are bound by this loop.
@@ -261,25 +289,24 @@ __device__ __forceinline__ void epi_store_block(const CUtensorMap* tmap_c, uint8
                    pack_half2_rn(__float_as_uint(f[6]), __float_as_uint(f[7])));
     }
   }
-  fence_proxy_async_smem();
+  epi_issue_store<NBUF>(tmap_c, buf, sbuf, lane, x, y, sc, x_end);
+}
+
+// epi_store_block for the plain product (alpha = 1, beta = 0) whose fp16
+// pairs are packed already: pk[w] holds columns 2w and 2w + 1 of the lane's
+// row, so the accumulator could be released before any store.
+template <int NBUF>
+__device__ __forceinline__ void epi_store_block_packed(const CUtensorMap* tmap_c, uint8_t* epi_buf, uint32_t epi_addr,
+                                                       int& sbuf, int lane, const uint32_t (&pk)[32], int x, int y,
+                                                       const EpiParams& sc, int x_end = 0x7fffffff) {
+  if (lane == 0) bulk_wait_group_read<NBUF - 1>();
   __syncwarp();
-  if (lane == 0 && tma_part) {
-    if (sc.c_evict_first)
-      tma_store_2d_hint(tmap_c, buf, x, y, policy_evict_first());
-    else
-      tma_store_2d(tmap_c, buf, x, y);
-    bulk_commit_group();
-  }
-  const int c_hi = x_end < sc.n ? x_end : sc.n;
-  if (!in_tile)
-    epi_plain_store(buf, lane, x, y, sc, x, c_hi, &sc.c, 1);
-  else if (sc.n_tma < sc.n && x + kEpiCols > sc.n_tma)
-    epi_plain_store(buf, lane, x, y, sc, sc.n_tma, sc.n, &sc.c, 1);
-  if (sc.n_peers > 0) epi_plain_store(buf, lane, x, y, sc, 0, c_hi, sc.peer, sc.n_peers);
-  // The ring advances with the bulk groups: a block past the map committed
-  // none, so its buffer (only read synchronously) is reused by the next block;
-  // otherwise the wait above would count one group short.
-  if (tma_part) sbuf = (sbuf + 1) % NBUF;
+  uint8_t* buf = epi_buf + sbuf * kEpiBufBytes;
+  const uint32_t row_addr = epi_addr + sbuf * kEpiBufBytes + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+  epi_issue_store<NBUF>(tmap_c, buf, sbuf, lane, x, y, sc, x_end);
 }
 
 // End of an epilogue warp in gathered-output mode: its peer stores are

@@ -671,6 +671,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
           continue;
         }
+        if (MSUB == 2 && sc.alpha == 1.0f && sc.beta == 0.0f) {
+          // Plain product, wide pair (one tile fills TMEM, so the next tile's
+          // MMAs wait for this block): the whole 256-column block goes to
+          // registers as packed fp16 and the accumulator is handed back
+          // before any store (measured 0.4-2 % faster than storing chunk by
+          // chunk first, 8192^3 to 4000 x 6000 x 3000).
+          uint32_t pk[Cfg::kChunksN][32];
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunksN; ++c) {
+            uint32_t lo[32], hi[32];
+            tmem_ld_32x32b_x32(t_row + c * kEpiCols, lo);
+            tmem_ld_32x32b_x32(t_row + c * kEpiCols + 32, hi);
+            tmem_ld_wait_regs(lo);
+            tmem_ld_wait_regs(hi);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              pk[c][e] = pack_half2_rn(lo[2 * e], lo[2 * e + 1]);
+              pk[c][16 + e] = pack_half2_rn(hi[2 * e], hi[2 * e + 1]);
+            }
+          }
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[buf * MSUB + s]), 0));
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunksN; ++c)
+            epi_store_block_packed<2>(&tmap_c, epi_buf, epi_addr, sbuf, lane, pk[c], n0 + c * kEpiCols,
+                                      m0 + quad * 32, sc, n0 + Cfg::kTileN);
+          continue;
+        }
 #pragma unroll 1
         for (int c = 0; c < Cfg::kChunksN; ++c) {
           uint32_t lo[32], hi[32];
