@@ -574,10 +574,12 @@ int wide_pair_bn(int m, int n, int slots, double* waves_out = nullptr) {
 
 int pick_tensor_variant(int m, int n, int k, int sm_count) {
   if (k < 512) return B200_VARIANT_CTA1;  // a pair's prologue is not amortised
-  // One wave of 1-CTA tiles: every variant takes about one tile's time and the
-  // 1-CTA kernel has the cheapest start (2048^3: 16.4-16.7 us against 17.3-17.6
-  // for the pair kernel).
-  if ((long long)((m + 127) / 128) * ((n + 255) / 256) <= sm_count) return B200_VARIANT_CTA1;
+  // One wave of 1-CTA tiles of moderate depth: every variant takes about one
+  // tile's time and the 1-CTA kernel has the cheapest start (2048^3: 16.4-16.7
+  // us against 17.3-17.6 for the pair kernel).  Deeper single-wave shapes go
+  // through the model below (1536 x 1280 x 8192: pair 44.7 us against 47.5
+  // for the 1-CTA kernel).
+  if (k <= 4096 && (long long)((m + 127) / 128) * ((n + 255) / 256) <= sm_count) return B200_VARIANT_CTA1;
   // Cost in SM cycles: waves x one tile's MMA time / relative rate, plus the
   // last tile's accumulator drain (one 256-column block, two for the wide pair).
   struct Opt {
@@ -586,7 +588,10 @@ int pick_tensor_variant(int m, int n, int k, int sm_count) {
   };
   const int pairs = sm_count / 2;
   const Opt opts[3] = {
-      {B200_VARIANT_PAIR_WIDE, 512, 256, pairs, 256, 1.00, 6400.0},
+      // Wide pair drain: 3200 cycles since its epilogue releases each
+      // accumulator block before storing it (3072^3: one wave of wide tiles
+      // 43.0 us against 45.0 for two waves of the pair kernel).
+      {B200_VARIANT_PAIR_WIDE, 512, 256, pairs, 256, 1.00, 3200.0},
       {B200_VARIANT_PAIR, 256, 256, pairs, 128, 0.96, 3200.0},
       {B200_VARIANT_CTA1, 128, 256, sm_count, 128, 0.93, 3200.0},
   };

@@ -132,6 +132,8 @@ def test_gather_argument_validation_without_gpu(native_lib):
     ((2560, 2048, 2048), "pair2m_192", 1),  # one wave of 55 tiles 192 wide (256 wide: 40 tiles on 80 SMs)
     ((4000, 6000, 3000), "pair2m", 1),    # narrower wide-pair tiles would not save a wave
     ((4096, 8192, 4096), "pair", 1),
+    ((3072, 3072, 3072), "pair2m", 1),    # one wave of wide tiles against two of the pair kernel
+    ((1536, 1280, 8192), "pair", 1),      # one wave, deep K: the pair kernel, not the 1-CTA one
 ])
 def test_launch_plan(native_lib, shape, variant, ranges):
     """The kernel choice (wave model) and last-wave split, computed on the host."""
